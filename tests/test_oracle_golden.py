@@ -1,0 +1,283 @@
+"""Pins the CPU oracle to the reference's own known-answer tests (tests/golden).
+
+The reference (Rust + Metal) cannot be built in this container, so these vectors, read out of
+its test sources, are what ties the oracle restatement to the reference's behaviour.
+"""
+import json
+import struct
+from pathlib import Path
+
+import numpy as np
+import pytest
+
+from oracle import oracle as O
+
+G = json.loads((Path(__file__).parent / "golden" / "reference_goldens.json").read_text())
+
+
+def f32(bits: str) -> np.float32:
+    return np.frombuffer(struct.pack("<I", int(bits, 16)), dtype=np.float32)[0]
+
+
+def bits_of(x) -> int:
+    return int(np.asarray(x, dtype=np.float32).view(np.uint32))
+
+
+def arr(case, key):
+    if key + "_bits" in case:
+        return np.array([f32(b) for b in case[key + "_bits"]], dtype=np.float32)
+    return np.array(case.get(key, []), dtype=np.float32)
+
+
+@pytest.mark.parametrize("case", G["gemm_f32"], ids=lambda c: c["cite"].split(" ")[0])
+def test_gemm_f32_goldens(case):
+    m, n, k = case["m"], case["n"], case["k"]
+    a = arr(case, "a").reshape(m, k)
+    b = arr(case, "b").reshape(k, n)
+    c = arr(case, "c0").reshape(m, n).copy()
+    c0 = c.copy()
+    alpha, beta = np.float32(case["alpha"]), np.float32(case["beta"])
+    O.gemm(O.DT_F32, a, b, c, alpha, beta)
+    if "expected" in case:
+        assert [bits_of(v) for v in c.ravel()] == [bits_of(v) for v in np.float32(case["expected"])]
+    if "expected_bits" in case:
+        assert [bits_of(v) for v in c.ravel()] == [int(x, 16) for x in case["expected_bits"]]
+    if case.get("expected_c00_formula"):
+        acc = np.float32(beta * c0[0, 0])
+        acc = np.float32(acc + np.float32(np.float32(alpha * a[0, 0]) * b[0, 0]))
+        acc = np.float32(acc + np.float32(np.float32(alpha * a[0, 1]) * b[1, 0]))
+        assert bits_of(c[0, 0]) == bits_of(acc)
+    if case.get("expected_left_assoc"):
+        left = np.float32(np.float32(alpha * a[0, 0]) * b[0, 0])
+        right = np.float32(alpha * np.float32(a[0, 0] * b[0, 0]))
+        assert bits_of(left) != bits_of(right)
+        assert bits_of(c[0, 0]) == bits_of(left)
+
+
+def test_gemm_transposed_layouts_match_row_major():
+    # crates/cpu/src/invariants.rs:100-134: the three layouts give the same bits.
+    rng = np.random.default_rng(3)
+    m, n, k = 5, 7, 11
+    a = rng.standard_normal((m, k)).astype(np.float32)
+    b = rng.standard_normal((k, n)).astype(np.float32)
+    ref = np.zeros((m, n), np.float32)
+    O.gemm(O.DT_F32, a, b, ref, 1.0, 0.0)
+    at = np.ascontiguousarray(a.T)  # storage [k, m]; the view has strides [1, m]
+    c1 = np.zeros((m, n), np.float32)
+    O.gemm(O.DT_F32, at, b, c1, 1.0, 0.0, a_strides=(1, m))
+    bt = np.ascontiguousarray(b.T)
+    c2 = np.zeros((m, n), np.float32)
+    O.gemm(O.DT_F32, a, bt, c2, 1.0, 0.0, b_strides=(1, k))
+    assert (ref.view(np.uint32) == c1.view(np.uint32)).all()
+    assert (ref.view(np.uint32) == c2.view(np.uint32)).all()
+
+
+def test_half_conversions():
+    h = G["half_conversions"]
+    for v, bits in h["f16"]:
+        assert O.f32_to_f16_bits(v) == int(bits, 16)
+    for v, bits in h["bf16"]:
+        assert int(O.f32_to_bf16(np.float32([v]))[0]) == int(bits, 16)
+
+
+@pytest.mark.parametrize("case", G["gemm_half"]["cases"])
+def test_gemm_half_goldens(case):
+    dt = O.DT_F16 if case["dtype"] == "f16" else O.DT_BF16
+
+    def enc(vals):
+        if dt == O.DT_F16:
+            return np.array([O.f32_to_f16_bits(v) for v in vals], dtype=np.uint16)
+        return O.f32_to_bf16(np.float32(vals))
+
+    k = len(case["a"])
+    a = enc(case["a"]).reshape(1, k)
+    b = enc(case["b"]).reshape(k, 1)
+    c = enc(case["c"]).reshape(1, 1).copy()
+    O.gemm(dt, a, b, c, case["alpha"], case["beta"])
+    assert int(c[0, 0]) == int(case["expected"], 16)
+
+
+def test_convert_f32_to_bf16_goldens():
+    cv = G["convert_f32_to_bf16"]
+    xs = np.array([f32(a) for a, _ in cv["cases"]], dtype=np.float32)
+    got = O.f32_to_bf16(xs)
+    assert [int(v) for v in got] == [int(b, 16) for _, b in cv["cases"]]
+    nans = np.array([f32(b) for b in cv["nan_inputs"]], dtype=np.float32)
+    for bits, g in zip(cv["nan_inputs"], O.f32_to_bf16(nans)):
+        g = int(g)
+        assert g & 0x7F80 == 0x7F80 and g & 0x007F != 0
+        assert g & 0x0040
+        assert g & 0x8000 == (int(bits, 16) >> 16) & 0x8000
+    allh = np.arange(65536, dtype=np.uint16)
+    back = O.bf16_to_f32(allh)
+    assert (back.view(np.uint32) == (allh.astype(np.uint32) << 16)).all()
+
+
+def test_sgd_step_bits():
+    # crates/cpu/src/training.rs:203-218
+    rng = np.random.default_rng(7)
+    w = rng.standard_normal(300).astype(np.float32)
+    g = rng.standard_normal(300).astype(np.float32)
+    lr = np.float32(1e-3)
+    w2, g2 = O.sgd_step(w, g, lr)
+    want = (w - (lr * g).astype(np.float32)).astype(np.float32)
+    assert (w2.view(np.uint32) == want.view(np.uint32)).all()
+    assert (g2.view(np.uint32) == 0).all()
+
+
+def test_mse_grad_matches_sequential_definition():
+    rng = np.random.default_rng(8)
+    y = rng.standard_normal(97).astype(np.float32)
+    t = rng.standard_normal(97).astype(np.float32)
+    loss, dy = O.mse_grad(y, t)
+    s = np.float32(0)
+    n = np.float32(97)
+    for i in range(97):
+        d = np.float32(y[i] - t[i])
+        s = np.float32(s + np.float32(d * d))
+        assert bits_of(dy[i]) == bits_of(np.float32(np.float32(2 * d) / n))
+    assert bits_of(np.float32(loss)) == bits_of(np.float32(s / n))
+
+
+def test_erf_constants():
+    assert [O.lib().or_erf_constant_bits(i) for i in range(6)] == [int(b, 16) for b in G["erf_constants"]["bits"]]
+
+
+def test_local_order_goldens():
+    lo = G["local_order"]
+    for c in lo["cases"]:
+        got = O.local_order(c["stages"], c["rank"], c["m"])
+        assert [f"{op}{m}" for op, m in got] == c["order"]
+    for s, r, m in lo["rejects"]:
+        assert O.local_order(s, r, m) is None
+
+
+def test_local_order_properties():
+    # crates/schedule/src/lib.rs:113-180
+    for stages in range(1, 6):
+        for rank in range(stages):
+            for m in range(1, 9):
+                order = O.local_order(stages, rank, m)
+                fs = [i for op, i in order if op == "F"]
+                bs = [i for op, i in order if op == "B"]
+                assert fs == list(range(m)) and bs == list(range(m))
+                for mb in range(m):
+                    assert order.index(("F", mb)) < order.index(("B", mb))
+
+
+def test_placement_goldens():
+    p = G["placement"]
+    for layers, stages, owners in p["cases"]:
+        assert O.contiguous_placement(layers, stages) == owners
+    for layers, stages in p["rejects"]:
+        assert O.contiguous_placement(layers, stages) is None
+
+
+@pytest.mark.parametrize("case", G["argmax"]["cases"])
+def test_argmax_goldens(case):
+    x = arr(case, "x")
+    assert O.argmax(x) == case["expected"]
+
+
+def test_argmax_nan_and_ties():
+    # tests/argmax_test.rs:316-362 style cases
+    x = np.ones(10, np.float32)
+    x[3] = np.inf
+    x[7] = np.nan
+    assert O.argmax(x) == 7
+    x[1] = -np.nan
+    assert O.argmax(x) == 1
+    y = np.full(9, 7.0, np.float32)
+    y[::2] = -7.0
+    assert O.argmax(y) == 0
+
+
+def test_sqrt_and_reciprocal_goldens():
+    for xb, yb in G["sqrt"]["cases"]:
+        assert bits_of(O.sqrt(np.array([f32(xb)]))[0]) == int(yb, 16)
+    s = G["reciprocal"]["simple"]
+    assert list(O.reciprocal(np.float32(s["x"]))) == s["y"]
+    xs = np.array([f32(a) for a, _ in G["reciprocal"]["cases"]], np.float32)
+    assert [bits_of(v) for v in O.reciprocal(xs)] == [int(b, 16) for _, b in G["reciprocal"]["cases"]]
+
+
+def test_wire_goldens():
+    w = G["wire"]
+    for c in w["roundtrip"]:
+        payload = bytes.fromhex(c["payload"])
+        msg = O.wire_header(c["dtype"], c["shape"]) + payload
+        assert msg[:4] == b"LNGL"
+        tag, shape, off = O.wire_parse(msg)
+        assert (tag, shape, msg[off:]) == (c["dtype"], c["shape"], payload)
+    for c in w["lengths"]:
+        nbytes = 4 if c["dtype"] == 1 else 2
+        for s in c["shape"]:
+            nbytes *= s
+        assert len(O.wire_header(c["dtype"], c["shape"])) + nbytes == c["len"]
+    for c in w["header_errors"]:
+        with pytest.raises(ValueError, match=c["error"]):
+            O.wire_header(c["dtype"], c["shape"])
+    good = O.wire_header(1, [1]) + b"\x11\x22\x33\x44"
+    for bad in (b"X" + good[1:], good[:4] + struct.pack("<I", 2) + good[8:], b"", b"\0" * 15, good[:16],
+                good[:-1], good + b"\xff"):
+        with pytest.raises(ValueError, match="Wire"):
+            O.wire_parse(bad)
+
+
+def _fixture_weights():
+    fx = G["pipeline_fixture"]
+    widths = fx["widths"]
+    ws = []
+    for l in range(len(widths) - 1):
+        w = np.zeros((widths[l], widths[l + 1]), np.float32)
+        for r in range(widths[l]):
+            for c in range(widths[l + 1]):
+                v = np.float32(np.float32(0.1) * np.float32(r + 1)) - np.float32(np.float32(0.05) * np.float32(c + 1))
+                w[r, c] = np.float32(np.float32(v) + np.float32(np.float32(0.02) * np.float32(l)))
+        ws.append(w)
+    return fx, widths, ws
+
+
+def test_train_reference_matches_hand_sequential():
+    """crates/pipeline/tests/pipeline.rs:396-480: the sequential reference over the tiny fixture,
+    restated with numpy f32 ops in the same order, equals the C restatement bit for bit."""
+    fx, widths, ws = _fixture_weights()
+    b = fx["batch"]
+    xs = [fx["x0"], fx["x1"]]
+    dys = [fx["dy0"], fx["dy1"]]
+    y, dw = O.train_reference("gelu", widths, b, ws, xs, dys)
+    # independent restatement with the oracle's gemm and gelu pieces, microbatch by microbatch
+    dws = [np.zeros_like(w) for w in ws]
+    for mb in range(2):
+        acts = [np.float32(xs[mb]).reshape(b, widths[0])]
+        pres = []
+        for l, w in enumerate(ws):
+            pre = np.zeros((b, widths[l + 1]), np.float32)
+            O.gemm(O.DT_F32, acts[-1], w, pre, 1.0, 0.0)
+            pres.append(pre)
+            acts.append(O.gelu(pre))
+        assert (acts[-1].view(np.uint32) == y[mb].view(np.uint32)).all()
+        g = np.float32(dys[mb]).reshape(b, widths[-1])
+        for l in reversed(range(len(ws))):
+            dpre = O.gelu_backward(pres[l], g)
+            O.gemm(O.DT_F32, np.ascontiguousarray(acts[l].T), dpre, dws[l], 1.0, 1.0)
+            dx = np.zeros((b, widths[l]), np.float32)
+            O.gemm(O.DT_F32, dpre, np.ascontiguousarray(ws[l].T), dx, 1.0, 0.0)
+            g = dx
+    for got, want in zip(dw, dws):
+        assert (got.view(np.uint32) == want.view(np.uint32)).all()
+
+
+def test_mlp_step_decreases_loss_and_is_thread_invariant():
+    rng = np.random.default_rng(11)
+    L, d, B, mb = 2, 32, 16, 4
+    master = (rng.standard_normal((L, d, d)) / np.sqrt(d)).astype(np.float32)
+    x = rng.standard_normal((B, d)).astype(np.float32)
+    t = rng.standard_normal((B, d)).astype(np.float32)
+    m1 = master.copy()
+    m2 = master.copy()
+    l1 = O.mlp_step(m1, x, t, mb, 0.5, threads=1)
+    l2 = O.mlp_step(m2, x, t, mb, 0.5, threads=3)
+    assert l1 == l2 and (m1.view(np.uint32) == m2.view(np.uint32)).all()
+    l3 = O.mlp_step(m1, x, t, mb, 0.5, threads=1)
+    assert l3 < l1
