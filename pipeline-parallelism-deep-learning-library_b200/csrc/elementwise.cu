@@ -1,0 +1,507 @@
+// elementwise.cu -- correctly rounded sqrt / reciprocal over strided views, and the Backend
+// training ops (add_bias, bias_grad, mse_grad, sgd_step, convert, gelu, relu and their
+// backwards).
+//
+// Bandwidth layout: a contiguous pair of views runs a 16-byte vector grid-stride loop sized to
+// the SM count (HBM-bound: 8 bytes moved per element); any other layout runs a per-element
+// mixed-radix decode over at most 8 merged axes.  All arithmetic is IEEE f32 with no flush to
+// zero and no FMA contraction (the library is built with -fmad=false), one rounding per
+// written operation, as crates/core/src/lib.rs:98-102 requires.
+#include <cuda_bf16.h>
+#include <cuda_runtime.h>
+
+#include <cmath>
+#include <cstring>
+#include <string>
+#include <vector>
+
+#include "internal.h"
+
+namespace {
+
+struct Strided {
+  int rank;
+  uint64_t count;
+  uint64_t src_off, dst_off;
+  uint64_t shape[LC_MAX_RANK];
+  uint64_t src_st[LC_MAX_RANK];
+  uint64_t dst_st[LC_MAX_RANK];
+};
+
+// Merges axes that are contiguous in both views (outer stride == inner stride * inner extent).
+Strided merge_pair(const lc_view& src, const lc_view& dst) {
+  Strided p{};
+  p.src_off = src.offset;
+  p.dst_off = dst.offset;
+  p.count = lc::numel(src);
+  int r = 0;
+  for (int d = 0; d < src.rank; d++) {
+    if (src.shape[d] == 1) continue;
+    if (r > 0 && p.src_st[r - 1] == src.strides[d] * src.shape[d] && p.dst_st[r - 1] == dst.strides[d] * src.shape[d]) {
+      p.shape[r - 1] *= src.shape[d];
+      p.src_st[r - 1] = src.strides[d];
+      p.dst_st[r - 1] = dst.strides[d];
+      continue;
+    }
+    p.shape[r] = src.shape[d];
+    p.src_st[r] = src.strides[d];
+    p.dst_st[r] = dst.strides[d];
+    r++;
+  }
+  if (r == 0) {
+    p.shape[0] = 1;
+    p.src_st[0] = 1;
+    p.dst_st[0] = 1;
+    r = 1;
+  }
+  p.rank = r;
+  return p;
+}
+
+__device__ __forceinline__ void decode(const Strided& p, uint64_t i, uint64_t* so, uint64_t* dof) {
+  uint64_t s = p.src_off, d = p.dst_off;
+  for (int a = p.rank - 1; a >= 0; a--) {
+    uint64_t n = p.shape[a];
+    uint64_t c = i % n;
+    i /= n;
+    s += c * p.src_st[a];
+    d += c * p.dst_st[a];
+  }
+  *so = s;
+  *dof = d;
+}
+
+// (x as f64).sqrt() as f32.  __fsqrt_rn is IEEE correctly rounded (no ftz in this build), which
+// equals the double-then-round value because 53 >= 2*24 + 2.  NaN inputs keep sign and payload
+// and become quiet, and a negative input gives the x86 default NaN 0xffc00000, as the Rust
+// expression does on the reference's hosts.
+__device__ __forceinline__ float sqrt_ref(float x) {
+  uint32_t b = __float_as_uint(x);
+  if ((b & 0x7fffffffu) > 0x7f800000u) return __uint_as_float(b | 0x00400000u);
+  if (x < 0.0f) return __uint_as_float(0xffc00000u);
+  return __fsqrt_rn(x);
+}
+
+// (1.0 / x as f64) as f32: __frcp_rn is the correctly rounded reciprocal (subnormal inputs and
+// results kept).  NaN keeps sign and payload and becomes quiet.
+__device__ __forceinline__ float rcp_ref(float x) {
+  uint32_t b = __float_as_uint(x);
+  if ((b & 0x7fffffffu) > 0x7f800000u) return __uint_as_float(b | 0x00400000u);
+  return __frcp_rn(x);
+}
+
+template <int OP>
+__device__ __forceinline__ float apply(float x) {
+  if constexpr (OP == 0) return sqrt_ref(x);
+  else return rcp_ref(x);
+}
+
+template <int OP>
+__global__ void __launch_bounds__(256) unary_vec_kernel(const float4* __restrict__ src, float4* __restrict__ dst,
+                                                         uint64_t n4) {
+  uint64_t i = blockIdx.x * (uint64_t)blockDim.x + threadIdx.x;
+  const uint64_t stride = (uint64_t)gridDim.x * blockDim.x;
+  // Four independent 16-byte loads in flight per thread before the first store.
+  for (; i + 3 * stride < n4; i += 4 * stride) {
+    float4 v[4];
+#pragma unroll
+    for (int u = 0; u < 4; u++) v[u] = __ldcs(src + i + u * stride);
+#pragma unroll
+    for (int u = 0; u < 4; u++) {
+      float4 r = make_float4(apply<OP>(v[u].x), apply<OP>(v[u].y), apply<OP>(v[u].z), apply<OP>(v[u].w));
+      __stcs(dst + i + u * stride, r);
+    }
+  }
+  for (; i < n4; i += stride) {
+    float4 v = __ldcs(src + i);
+    __stcs(dst + i, make_float4(apply<OP>(v.x), apply<OP>(v.y), apply<OP>(v.z), apply<OP>(v.w)));
+  }
+}
+
+template <int OP>
+__global__ void unary_scalar_kernel(const float* __restrict__ src, float* __restrict__ dst, uint64_t n) {
+  uint64_t i = blockIdx.x * (uint64_t)blockDim.x + threadIdx.x;
+  if (i < n) dst[i] = apply<OP>(src[i]);
+}
+
+template <int OP>
+__global__ void unary_strided_kernel(const float* src, float* dst, Strided p) {
+  const uint64_t stride = (uint64_t)gridDim.x * blockDim.x;
+  for (uint64_t i = blockIdx.x * (uint64_t)blockDim.x + threadIdx.x; i < p.count; i += stride) {
+    uint64_t so, dof;
+    decode(p, i, &so, &dof);
+    dst[dof] = apply<OP>(src[so]);
+  }
+}
+
+unsigned grid_for(lc_context* ctx, uint64_t work, unsigned block) {
+  uint64_t want = (work + block - 1) / block;
+  uint64_t cap = (uint64_t)ctx->sm_count * 8;
+  if (want > cap) want = cap;
+  if (want == 0) want = 1;
+  return (unsigned)want;
+}
+
+template <int OP>
+lc_status run_unary(lc_context* ctx, void* stream, const lc_view* srcp, const lc_view* dstp, const char* opname) {
+  using namespace lc;
+  if (ctx == nullptr || srcp == nullptr || dstp == nullptr) return fail(LC_ERR_INVALID_ARGUMENT, "null argument");
+  const lc_view& src = *srcp;
+  const lc_view& dst = *dstp;
+  // src/ops/sqrt.rs:121-167 `prepare` order: validate, dtype, shape, rank, overlap, empty,
+  // injective destination.
+  lc_status st = validate(src, "src");
+  if (st) return st;
+  if ((st = validate(dst, "dst"))) return st;
+  if (src.dtype != LC_F32 || dst.dtype != LC_F32)
+    return fail(LC_ERR_INVALID_ARGUMENT, std::string(opname) + " supports real f32 views");
+  if (src.rank != dst.rank || memcmp(src.shape, dst.shape, sizeof(uint64_t) * src.rank) != 0)
+    return fail(LC_ERR_INVALID_ARGUMENT, std::string(opname) + " shape mismatch");
+  bool inplace = same_view(src, dst);
+  if (!inplace && may_overlap(src, dst))
+    return fail(LC_ERR_OVERLAP, std::string(opname) +
+                                    " views overlap; in-place requires the same buffer, offset, shape, and strides");
+  if (is_empty(src)) return LC_OK;
+  if (!is_injective(dst))
+    return fail(LC_ERR_INVALID_ARGUMENT, std::string(opname) + " destination is not injective; parallel stores would alias");
+  cudaStream_t s = stream_of(ctx, stream);
+  const float* sp = static_cast<const float*>(src.data) + src.offset;
+  float* dp = static_cast<float*>(dst.data) + dst.offset;
+  uint64_t n = numel(src);
+  if (is_contiguous(src) && is_contiguous(dst)) {
+    bool aligned = (reinterpret_cast<uintptr_t>(sp) % 16 == 0) && (reinterpret_cast<uintptr_t>(dp) % 16 == 0);
+    if (aligned && n >= 4) {
+      uint64_t n4 = n / 4;
+      unary_vec_kernel<OP><<<grid_for(ctx, n4, 256) * 1, 256, 0, s>>>(reinterpret_cast<const float4*>(sp),
+                                                                       reinterpret_cast<float4*>(dp), n4);
+      record_launch(ctx, OP == 0 ? "sqrt_vec" : "reciprocal_vec");
+      uint64_t tail = n - n4 * 4;
+      if (tail) {
+        unary_scalar_kernel<OP><<<1, 32, 0, s>>>(sp + n4 * 4, dp + n4 * 4, tail);
+        record_launch(ctx, OP == 0 ? "sqrt_tail" : "reciprocal_tail");
+      }
+    } else {
+      unary_scalar_kernel<OP><<<(unsigned)((n + 255) / 256), 256, 0, s>>>(sp, dp, n);
+      record_launch(ctx, OP == 0 ? "sqrt_scalar" : "reciprocal_scalar");
+    }
+  } else {
+    Strided p = merge_pair(src, dst);
+    unary_strided_kernel<OP><<<grid_for(ctx, n, 256), 256, 0, s>>>(static_cast<const float*>(src.data),
+                                                                  static_cast<float*>(dst.data), p);
+    record_launch(ctx, OP == 0 ? "sqrt_strided" : "reciprocal_strided");
+  }
+  cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess) return cuda_fail(e, opname);
+  return LC_OK;
+}
+
+// ---------------------------------------------------------------------------------------------
+// Backend training ops (crates/cuda/train.cu semantics, crates/cpu/src/lib.rs:372-533 math).
+// ---------------------------------------------------------------------------------------------
+
+__global__ void add_bias_kernel(const float* x, const float* b, float* y, uint64_t rows, uint64_t cols) {
+  const uint64_t n = rows * cols, stride = (uint64_t)gridDim.x * blockDim.x;
+  for (uint64_t i = blockIdx.x * (uint64_t)blockDim.x + threadIdx.x; i < n; i += stride)
+    y[i] = __fadd_rn(x[i], b[i % cols]);
+}
+
+// Column sums in row order (the reference's order), one thread per column, then db += s.
+__global__ void bias_grad_kernel(const float* dpre, float* db, uint64_t rows, uint64_t cols) {
+  uint64_t c = blockIdx.x * (uint64_t)blockDim.x + threadIdx.x;
+  if (c >= cols) return;
+  float s = 0.0f;
+  for (uint64_t r = 0; r < rows; r++) s = __fadd_rn(s, dpre[r * cols + c]);
+  db[c] = __fadd_rn(db[c], s);
+}
+
+// mse_grad stage 1: dy = (2*d)/n exactly as the reference (bitwise), and per-block partial sums
+// of d*d in a fixed tree order (deterministic; the order differs from the reference's
+// sequential sum, so the loss matches within rounding).
+constexpr int kMseBlock = 512;
+__global__ void __launch_bounds__(kMseBlock) mse_stage1(const float* y, const float* t, float* dy, uint64_t n, float nf,
+                                                         float* partials) {
+  __shared__ float red[kMseBlock];
+  float acc = 0.0f;
+  const uint64_t stride = (uint64_t)gridDim.x * blockDim.x;
+  for (uint64_t i = blockIdx.x * (uint64_t)blockDim.x + threadIdx.x; i < n; i += stride) {
+    float d = __fsub_rn(y[i], t[i]);
+    acc = __fadd_rn(acc, __fmul_rn(d, d));
+    dy[i] = __fdiv_rn(__fmul_rn(2.0f, d), nf);
+  }
+  red[threadIdx.x] = acc;
+  __syncthreads();
+  for (int w = kMseBlock / 2; w > 0; w >>= 1) {
+    if (threadIdx.x < w) red[threadIdx.x] = __fadd_rn(red[threadIdx.x], red[threadIdx.x + w]);
+    __syncthreads();
+  }
+  if (threadIdx.x == 0) partials[blockIdx.x] = red[0];
+}
+
+__global__ void __launch_bounds__(kMseBlock) mse_stage2(const float* partials, int count, float nf, float* loss) {
+  __shared__ float red[kMseBlock];
+  float acc = 0.0f;
+  for (int i = threadIdx.x; i < count; i += kMseBlock) acc = __fadd_rn(acc, partials[i]);
+  red[threadIdx.x] = acc;
+  __syncthreads();
+  for (int w = kMseBlock / 2; w > 0; w >>= 1) {
+    if (threadIdx.x < w) red[threadIdx.x] = __fadd_rn(red[threadIdx.x], red[threadIdx.x + w]);
+    __syncthreads();
+  }
+  if (threadIdx.x == 0) *loss = __fdiv_rn(red[0], nf);
+}
+
+__global__ void sgd_kernel(float* w, float* dw, uint64_t n, float lr) {
+  const uint64_t stride = (uint64_t)gridDim.x * blockDim.x;
+  for (uint64_t i = blockIdx.x * (uint64_t)blockDim.x + threadIdx.x; i < n; i += stride) {
+    float step = __fmul_rn(lr, dw[i]);
+    w[i] = __fsub_rn(w[i], step);
+    dw[i] = 0.0f;
+  }
+}
+
+// crates/cpu/src/lib.rs:725-731 f32_bits_to_bf16.
+__device__ __forceinline__ uint16_t f32_to_bf16_bits(float x) {
+  uint32_t bits = __float_as_uint(x);
+  if ((bits & 0x7fffffffu) > 0x7f800000u) return (uint16_t)((bits >> 16) | 0x0040u);
+  uint32_t lsb = (bits >> 16) & 1u;
+  return (uint16_t)((bits + 0x7fffu + lsb) >> 16);
+}
+
+__global__ void convert_f32_bf16_kernel(const float* x, uint16_t* y, uint64_t n) {
+  const uint64_t stride = (uint64_t)gridDim.x * blockDim.x;
+  for (uint64_t i = blockIdx.x * (uint64_t)blockDim.x + threadIdx.x; i < n; i += stride) y[i] = f32_to_bf16_bits(x[i]);
+}
+
+__global__ void convert_bf16_f32_kernel(const uint16_t* x, float* y, uint64_t n) {
+  const uint64_t stride = (uint64_t)gridDim.x * blockDim.x;
+  for (uint64_t i = blockIdx.x * (uint64_t)blockDim.x + threadIdx.x; i < n; i += stride)
+    y[i] = __uint_as_float(((uint32_t)x[i]) << 16);
+}
+
+// GELU with the reference's Abramowitz-Stegun 7.1.26 erf, in f32 (crates/cpu/src/lib.rs:809-853).
+__device__ __forceinline__ float erf_as(float x) {
+  const float A1 = 0.254829592f, A2 = 0.284496736f, A3 = 1.421413741f, A4 = 1.453152027f, A5 = 1.061405429f;
+  float sign = signbit(x) ? -1.0f : 1.0f;
+  x = fabsf(x);
+  float t = __fdiv_rn(1.0f, __fadd_rn(1.0f, __fmul_rn(0.3275911f, x)));
+  float poly = __fmul_rn(A5, t);
+  poly = __fmul_rn(__fsub_rn(poly, A4), t);
+  poly = __fmul_rn(__fadd_rn(poly, A3), t);
+  poly = __fmul_rn(__fsub_rn(poly, A2), t);
+  poly = __fmul_rn(__fadd_rn(poly, A1), t);
+  return __fmul_rn(sign, __fsub_rn(1.0f, __fmul_rn(poly, expf(-__fmul_rn(x, x)))));
+}
+
+__device__ __forceinline__ float gelu1(float x) {
+  return __fmul_rn(__fmul_rn(0.5f, x), __fadd_rn(1.0f, erf_as(__fmul_rn(x, 0.70710678118654752440f))));
+}
+
+__device__ __forceinline__ float gelu_prime1(float x) {
+  float phi = __fmul_rn(0.5f, __fadd_rn(1.0f, erf_as(__fmul_rn(x, 0.70710678118654752440f))));
+  float pdf = __fmul_rn(expf(__fmul_rn(__fmul_rn(-0.5f, x), x)), 0.3989422804014327f);
+  return __fadd_rn(phi, __fmul_rn(x, pdf));
+}
+
+template <int OP>  // 0 gelu, 1 relu
+__global__ void act_kernel(const float* x, float* y, uint64_t n) {
+  const uint64_t stride = (uint64_t)gridDim.x * blockDim.x;
+  for (uint64_t i = blockIdx.x * (uint64_t)blockDim.x + threadIdx.x; i < n; i += stride) {
+    float v = x[i];
+    y[i] = OP == 0 ? gelu1(v) : (v > 0.0f ? v : 0.0f);
+  }
+}
+
+template <int OP>
+__global__ void act_backward_kernel(const float* pre, const float* dy, float* dx, uint64_t n) {
+  const uint64_t stride = (uint64_t)gridDim.x * blockDim.x;
+  for (uint64_t i = blockIdx.x * (uint64_t)blockDim.x + threadIdx.x; i < n; i += stride) {
+    float p = pre[i];
+    dx[i] = OP == 0 ? __fmul_rn(dy[i], gelu_prime1(p)) : (p > 0.0f ? dy[i] : 0.0f);
+  }
+}
+
+// ---- shared checks in the order Shape, Dtype, Alias, UnsupportedLayout ----------------------
+
+bool shape_eq(const lc_view& a, const lc_view& b) {
+  return a.rank == b.rank && memcmp(a.shape, b.shape, sizeof(uint64_t) * a.rank) == 0;
+}
+
+lc_status check_training(std::initializer_list<const lc_view*> all) {
+  using namespace lc;
+  for (const lc_view* v : all) {
+    if (!packed_layout(*v)) return fail(LC_ERR_UNSUPPORTED_LAYOUT, "operand is not row-major contiguous at offset 0");
+    uint64_t need = numel(*v) * dtype_size(v->dtype);
+    if (need > v->buffer_bytes) return fail(LC_ERR_SHAPE, "buffer is shorter than the tensor");
+  }
+  return LC_OK;
+}
+
+lc_status launched(lc_context* ctx, const char* name) {
+  lc::record_launch(ctx, name);
+  cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess) return lc::cuda_fail(e, name);
+  return LC_OK;
+}
+
+}  // namespace
+
+using namespace lc;
+
+extern "C" {
+
+lc_status lc_encode_sqrt(lc_context* ctx, void* stream, const lc_view* src, const lc_view* dst) {
+  return run_unary<0>(ctx, stream, src, dst, "sqrt");
+}
+
+lc_status lc_sqrt(lc_context* ctx, const lc_view* src, const lc_view* dst) {
+  lc_status st = lc_encode_sqrt(ctx, nullptr, src, dst);
+  return st ? st : lc_sync(ctx, nullptr);
+}
+
+lc_status lc_encode_reciprocal(lc_context* ctx, void* stream, const lc_view* src, const lc_view* dst) {
+  return run_unary<1>(ctx, stream, src, dst, "reciprocal");
+}
+
+lc_status lc_reciprocal(lc_context* ctx, const lc_view* src, const lc_view* dst) {
+  lc_status st = lc_encode_reciprocal(ctx, nullptr, src, dst);
+  return st ? st : lc_sync(ctx, nullptr);
+}
+
+lc_status lc_add_bias(lc_context* ctx, void* stream, const lc_view* x, const lc_view* b, const lc_view* y) {
+  if (!ctx || !x || !b || !y) return fail(LC_ERR_INVALID_ARGUMENT, "null argument");
+  if (x->rank != 2 || !shape_eq(*x, *y) || b->rank != 1 || b->shape[0] != x->shape[1])
+    return fail(LC_ERR_SHAPE, "add_bias: x [B,N], b [N], y [B,N]");
+  if (x->dtype != LC_F32 || b->dtype != LC_F32 || y->dtype != LC_F32) return fail(LC_ERR_DTYPE, "add_bias: f32 only");
+  if (b->data == x->data || b->data == y->data) return fail(LC_ERR_ALIAS, "add_bias: b shares storage");
+  lc_status st = check_training({x, b, y});
+  if (st) return st;
+  uint64_t n = numel(*x);
+  cudaStream_t s = stream_of(ctx, stream);
+  add_bias_kernel<<<grid_for(ctx, n, 256), 256, 0, s>>>((const float*)x->data, (const float*)b->data, (float*)y->data,
+                                                        x->shape[0], x->shape[1]);
+  return launched(ctx, "add_bias");
+}
+
+lc_status lc_bias_grad(lc_context* ctx, void* stream, const lc_view* dpre, const lc_view* db) {
+  if (!ctx || !dpre || !db) return fail(LC_ERR_INVALID_ARGUMENT, "null argument");
+  if (dpre->rank != 2 || db->rank != 1 || db->shape[0] != dpre->shape[1])
+    return fail(LC_ERR_SHAPE, "bias_grad: dpre [B,N], db [N]");
+  if (dpre->dtype != LC_F32 || db->dtype != LC_F32) return fail(LC_ERR_DTYPE, "bias_grad: f32 only");
+  if (dpre->data == db->data) return fail(LC_ERR_ALIAS, "bias_grad: db shares storage with dpre");
+  lc_status st = check_training({dpre, db});
+  if (st) return st;
+  if (dpre->shape[0] == 0 || dpre->shape[1] == 0) {
+    record_launch(ctx, "bias_grad");
+    return LC_OK;
+  }
+  uint64_t cols = dpre->shape[1];
+  bias_grad_kernel<<<(unsigned)((cols + 255) / 256), 256, 0, stream_of(ctx, stream)>>>(
+      (const float*)dpre->data, (float*)db->data, dpre->shape[0], cols);
+  return launched(ctx, "bias_grad");
+}
+
+lc_status lc_mse_grad(lc_context* ctx, void* stream, const lc_view* y, const lc_view* target, const lc_view* dy,
+                      float* loss) {
+  if (!ctx || !y || !target || !dy || !loss) return fail(LC_ERR_INVALID_ARGUMENT, "null argument");
+  if (!shape_eq(*y, *target) || !shape_eq(*y, *dy)) return fail(LC_ERR_SHAPE, "mse_grad: shapes differ");
+  uint64_t n = numel(*y);
+  if (n == 0) return fail(LC_ERR_SHAPE, "mse_grad: empty tensor");
+  if (y->dtype != LC_F32 || target->dtype != LC_F32 || dy->dtype != LC_F32) return fail(LC_ERR_DTYPE, "mse_grad: f32 only");
+  if (dy->data == target->data) return fail(LC_ERR_ALIAS, "mse_grad: dy shares storage with target");
+  lc_status st = check_training({y, target, dy});
+  if (st) return st;
+  cudaStream_t s = stream_of(ctx, stream);
+  int blocks = (int)grid_for(ctx, n, kMseBlock);
+  float* scratch = nullptr;
+  if ((st = scratch_alloc(ctx, s, sizeof(float) * (blocks + 1), (void**)&scratch))) return st;
+  float nf = (float)n;
+  mse_stage1<<<blocks, kMseBlock, 0, s>>>((const float*)y->data, (const float*)target->data, (float*)dy->data, n, nf,
+                                          scratch + 1);
+  if ((st = launched(ctx, "mse_grad_partial"))) return st;
+  mse_stage2<<<1, kMseBlock, 0, s>>>(scratch + 1, blocks, nf, scratch);
+  if ((st = launched(ctx, "mse_grad_final"))) return st;
+  float h = 0.0f;
+  cudaError_t e = cudaMemcpyAsync(&h, scratch, sizeof(float), cudaMemcpyDeviceToHost, s);
+  scratch_free(scratch, s);
+  if (e == cudaSuccess) e = cudaStreamSynchronize(s);
+  if (e != cudaSuccess) return cuda_fail(e, "mse_grad loss readback");
+  *loss = h;
+  return LC_OK;
+}
+
+lc_status lc_sgd_step(lc_context* ctx, void* stream, const lc_view* w, const lc_view* dw, float lr) {
+  if (!ctx || !w || !dw) return fail(LC_ERR_INVALID_ARGUMENT, "null argument");
+  if (!shape_eq(*w, *dw)) return fail(LC_ERR_SHAPE, "sgd_step: shapes differ");
+  if (w->dtype != LC_F32 || dw->dtype != LC_F32) return fail(LC_ERR_DTYPE, "sgd_step: f32 only");
+  if (w->data == dw->data) return fail(LC_ERR_ALIAS, "sgd_step: w and dw share storage");
+  lc_status st = check_training({w, dw});
+  if (st) return st;
+  uint64_t n = numel(*w);
+  sgd_kernel<<<grid_for(ctx, n, 256), 256, 0, stream_of(ctx, stream)>>>((float*)w->data, (float*)dw->data, n, lr);
+  return launched(ctx, "sgd_step");
+}
+
+lc_status lc_convert(lc_context* ctx, void* stream, const lc_view* x, const lc_view* y) {
+  if (!ctx || !x || !y) return fail(LC_ERR_INVALID_ARGUMENT, "null argument");
+  if (!shape_eq(*x, *y)) return fail(LC_ERR_SHAPE, "convert: shapes differ");
+  bool f2b = x->dtype == LC_F32 && y->dtype == LC_BF16;
+  bool b2f = x->dtype == LC_BF16 && y->dtype == LC_F32;
+  if (!f2b && !b2f) return fail(LC_ERR_DTYPE, "convert: (f32, bf16) or (bf16, f32)");
+  if (x->data == y->data) return fail(LC_ERR_ALIAS, "convert: x and y share storage");
+  lc_status st = check_training({x, y});
+  if (st) return st;
+  uint64_t n = numel(*x);
+  cudaStream_t s = stream_of(ctx, stream);
+  if (f2b) {
+    convert_f32_bf16_kernel<<<grid_for(ctx, n, 256), 256, 0, s>>>((const float*)x->data, (uint16_t*)y->data, n);
+    return launched(ctx, "convert_f32_bf16");
+  }
+  convert_bf16_f32_kernel<<<grid_for(ctx, n, 256), 256, 0, s>>>((const uint16_t*)x->data, (float*)y->data, n);
+  return launched(ctx, "convert_bf16_f32");
+}
+
+static lc_status unary_training(lc_context* ctx, void* stream, const lc_view* x, const lc_view* y, int op) {
+  if (!ctx || !x || !y) return fail(LC_ERR_INVALID_ARGUMENT, "null argument");
+  if (x->dtype != LC_F32 || y->dtype != LC_F32) return fail(LC_ERR_DTYPE, "f32 only");
+  if (!shape_eq(*x, *y)) return fail(LC_ERR_SHAPE, "shapes differ");
+  lc_status st = check_training({x, y});
+  if (st) return st;
+  uint64_t n = numel(*x);
+  cudaStream_t s = stream_of(ctx, stream);
+  if (op == 0) act_kernel<0><<<grid_for(ctx, n, 256), 256, 0, s>>>((const float*)x->data, (float*)y->data, n);
+  else act_kernel<1><<<grid_for(ctx, n, 256), 256, 0, s>>>((const float*)x->data, (float*)y->data, n);
+  return launched(ctx, op == 0 ? "gelu" : "relu");
+}
+
+static lc_status backward_training(lc_context* ctx, void* stream, const lc_view* pre, const lc_view* dy,
+                                   const lc_view* dx, int op) {
+  if (!ctx || !pre || !dy || !dx) return fail(LC_ERR_INVALID_ARGUMENT, "null argument");
+  if (pre->dtype != LC_F32 || dy->dtype != LC_F32 || dx->dtype != LC_F32) return fail(LC_ERR_DTYPE, "f32 only");
+  if (!shape_eq(*pre, *dy) || !shape_eq(*pre, *dx)) return fail(LC_ERR_SHAPE, "shapes differ");
+  lc_status st = check_training({pre, dy, dx});
+  if (st) return st;
+  uint64_t n = numel(*pre);
+  cudaStream_t s = stream_of(ctx, stream);
+  if (op == 0)
+    act_backward_kernel<0><<<grid_for(ctx, n, 256), 256, 0, s>>>((const float*)pre->data, (const float*)dy->data,
+                                                                (float*)dx->data, n);
+  else
+    act_backward_kernel<1><<<grid_for(ctx, n, 256), 256, 0, s>>>((const float*)pre->data, (const float*)dy->data,
+                                                                (float*)dx->data, n);
+  return launched(ctx, op == 0 ? "gelu_backward" : "relu_backward");
+}
+
+lc_status lc_gelu(lc_context* ctx, void* stream, const lc_view* x, const lc_view* y) {
+  return unary_training(ctx, stream, x, y, 0);
+}
+lc_status lc_relu(lc_context* ctx, void* stream, const lc_view* x, const lc_view* y) {
+  return unary_training(ctx, stream, x, y, 1);
+}
+lc_status lc_gelu_backward(lc_context* ctx, void* stream, const lc_view* pre, const lc_view* dy, const lc_view* dx) {
+  return backward_training(ctx, stream, pre, dy, dx, 0);
+}
+lc_status lc_relu_backward(lc_context* ctx, void* stream, const lc_view* pre, const lc_view* dy, const lc_view* dx) {
+  return backward_training(ctx, stream, pre, dy, dx, 1);
+}
+
+}  // extern "C"

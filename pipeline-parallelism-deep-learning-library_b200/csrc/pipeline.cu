@@ -1,0 +1,724 @@
+// pipeline.cu -- 1F1B pipeline training, one stage per GPU, activations and gradients moved by
+// NCCL send/recv over NVLink on dedicated streams (crates/pipeline/src/lib.rs:100-230 rebuilt).
+//
+// Streams per stage: the compute stream (all kernels), a forward-transfer stream and a
+// backward-transfer stream.  Each transfer direction has its own communicator (the backward one
+// is split from the forward one), so on each communicator a rank's operations form a one-way
+// chain (forward: recv from r-1 then send to r+1, microbatch by microbatch) and can never wait on
+// each other in a cycle.  CUDA events order compute against transfers; the compute stream never
+// waits on a send, so sends behave like the reference's buffered transport.
+//
+// Training mode (the benchmark step; bf16 compute weights, f32 masters, ReLU, MSE, SGD):
+//   forward  H[l+1] = relu(H[l] @ Wb_l)              one GEMM, ReLU fused in the epilogue
+//   loss     dP[L-1] = bf16(2(y-t)/N) where y > 0    one kernel, deterministic partial sums
+//   backward dP[l-1] = (dP[l] @ Wb_l^T) where H[l] > 0 one GEMM, ReLU' mask fused (H[l] is the
+//            layer's stashed input); the mask for a stage's last layer is applied by the next
+//            stage before it sends, so no mask crosses the link; rank 0 skips layer 0's dgrad
+//   update   W_l -= lr * (H[l]^T @ dP[l]) over the whole batch (K = B), Wb_l = bf16(W_l), one
+//            GEMM per layer with the SGD fused into its epilogue (no dW buffer at all)
+// Reference mode (f32, GELU or ReLU, dy given): the reference's own dataflow with separate
+// activation kernels and dW += x^T dpre per microbatch (beta = 1), exactly as `train` orders it.
+#include <cuda_bf16.h>
+#include <cuda_runtime.h>
+#include <nccl.h>
+
+#include <chrono>
+#include <cstring>
+#include <string>
+#include <thread>
+#include <vector>
+
+#include "gemm.h"
+#include "internal.h"
+
+namespace {
+
+using namespace lc;
+
+// ---- kernels ----------------------------------------------------------------------------------
+
+__device__ __forceinline__ uint16_t bf16_bits(float x) {
+  uint32_t bits = __float_as_uint(x);
+  if ((bits & 0x7fffffffu) > 0x7f800000u) return (uint16_t)((bits >> 16) | 0x0040u);
+  uint32_t lsb = (bits >> 16) & 1u;
+  return (uint16_t)((bits + 0x7fffu + lsb) >> 16);
+}
+
+__device__ __forceinline__ float bf16_f32(uint16_t h) { return __uint_as_float(((uint32_t)h) << 16); }
+
+__global__ void to_bf16_kernel(const float* __restrict__ x, uint16_t* __restrict__ y, uint64_t n) {
+  const uint64_t stride = (uint64_t)gridDim.x * blockDim.x;
+  for (uint64_t i = blockIdx.x * (uint64_t)blockDim.x + threadIdx.x; i < n; i += stride) y[i] = bf16_bits(x[i]);
+}
+
+// MSE over the whole batch with the ReLU' of the last layer folded in:
+//   d = f32(y) - t;  part += d*d;  g = (y > 0) ? bf16((2*d)/N) : 0
+constexpr int kMseThreads = 256;
+constexpr int kMseBlocks = 64;
+__global__ void __launch_bounds__(kMseThreads) mse_relu_kernel(const uint16_t* __restrict__ y, const float* __restrict__ t,
+                                                                uint16_t* __restrict__ g, uint64_t n, float n_total,
+                                                                float* __restrict__ part) {
+  __shared__ float red[kMseThreads];
+  float acc = 0.0f;
+  const uint64_t stride = (uint64_t)gridDim.x * blockDim.x;
+  for (uint64_t i = blockIdx.x * (uint64_t)blockDim.x + threadIdx.x; i < n; i += stride) {
+    const float yv = bf16_f32(y[i]);
+    const float d = __fsub_rn(yv, t[i]);
+    acc = __fadd_rn(acc, __fmul_rn(d, d));
+    g[i] = yv > 0.0f ? bf16_bits(__fdiv_rn(__fmul_rn(2.0f, d), n_total)) : (uint16_t)0;
+  }
+  red[threadIdx.x] = acc;
+  __syncthreads();
+  for (int w = kMseThreads / 2; w > 0; w >>= 1) {
+    if (threadIdx.x < w) red[threadIdx.x] = __fadd_rn(red[threadIdx.x], red[threadIdx.x + w]);
+    __syncthreads();
+  }
+  if (threadIdx.x == 0) part[blockIdx.x] = red[0];
+}
+
+__global__ void __launch_bounds__(kMseThreads) loss_reduce_kernel(const float* __restrict__ part, int count, float n_total,
+                                                                   float* __restrict__ loss) {
+  __shared__ float red[kMseThreads];
+  float acc = 0.0f;
+  for (int i = threadIdx.x; i < count; i += kMseThreads) acc = __fadd_rn(acc, part[i]);
+  red[threadIdx.x] = acc;
+  __syncthreads();
+  for (int w = kMseThreads / 2; w > 0; w >>= 1) {
+    if (threadIdx.x < w) red[threadIdx.x] = __fadd_rn(red[threadIdx.x], red[threadIdx.x + w]);
+    __syncthreads();
+  }
+  if (threadIdx.x == 0) *loss = __fdiv_rn(red[0], n_total);
+}
+
+// N(0, stddev^2) from SplitMix64 draws 2i and 2i+1 of `seed` (Box-Muller, one rounding to f32).
+__device__ __forceinline__ uint64_t splitmix(uint64_t seed, uint64_t i) {
+  uint64_t z = seed + (i + 1) * 0x9E3779B97F4A7C15ull;
+  z = (z ^ (z >> 30)) * 0xBF58476D1CE4E5B9ull;
+  z = (z ^ (z >> 27)) * 0x94D049BB133111EBull;
+  return z ^ (z >> 31);
+}
+
+__global__ void normal_init_kernel(float* __restrict__ w, uint16_t* __restrict__ wb, uint64_t n, uint64_t seed,
+                                   float stddev) {
+  const uint64_t stride = (uint64_t)gridDim.x * blockDim.x;
+  for (uint64_t i = blockIdx.x * (uint64_t)blockDim.x + threadIdx.x; i < n; i += stride) {
+    const double u1 = ((double)(splitmix(seed, 2 * i) >> 11) + 1.0) * 0x1.0p-53;
+    const double u2 = (double)(splitmix(seed, 2 * i + 1) >> 11) * 0x1.0p-53;
+    const double z = sqrt(-2.0 * log(u1)) * cospi(2.0 * u2);
+    const float v = (float)(z * (double)stddev);
+    w[i] = v;
+    if (wb) wb[i] = bf16_bits(v);
+  }
+}
+
+unsigned blocks_for(lc_context* ctx, uint64_t n, unsigned per = 256) {
+  uint64_t b = (n + per - 1) / per;
+  uint64_t cap = (uint64_t)ctx->sm_count * 8;
+  return (unsigned)std::max<uint64_t>(1, std::min(b, cap));
+}
+
+// ---- helpers -----------------------------------------------------------------------------------
+
+lc_status nccl_fail(ncclResult_t r, const char* what) {
+  return fail(LC_ERR_TRANSPORT, std::string(what) + ": " + ncclGetErrorString(r));
+}
+
+#define CU(x)                                          \
+  do {                                                 \
+    cudaError_t e_ = (x);                              \
+    if (e_ != cudaSuccess) return cuda_fail(e_, #x);   \
+  } while (0)
+#define NC(x)                                          \
+  do {                                                 \
+    ncclResult_t r_ = (x);                             \
+    if (r_ != ncclSuccess) return nccl_fail(r_, #x);   \
+  } while (0)
+
+lc_view matrix_view(void* data, int32_t dtype, uint64_t rows, uint64_t cols, uint64_t buffer_bytes) {
+  lc_view v{};
+  v.data = data;
+  v.buffer_bytes = buffer_bytes;
+  v.dtype = dtype;
+  v.rank = 2;
+  v.shape[0] = rows;
+  v.shape[1] = cols;
+  v.strides[0] = cols;
+  v.strides[1] = 1;
+  return v;
+}
+
+}  // namespace
+
+struct lc_pipeline {
+  lc_pipeline_config cfg{};
+  std::vector<uint64_t> widths;  // global, layers + 1
+  int rank = 0, world = 1, device = 0;
+  bool train_mode = false;
+  lc_context* ctx = nullptr;
+  cudaStream_t s_fwd = nullptr, s_bwd = nullptr;
+  ncclComm_t comm_fwd = nullptr, comm_bwd = nullptr;
+  uint64_t first = 0, count = 0, B = 0;
+  std::vector<float*> master, dw, pre;
+  std::vector<void*> wb, H, dP;
+  void* gsend = nullptr;       // backward send buffer (rank > 0)
+  void* dbuf = nullptr;        // reference mode: per-microbatch dpre / dx scratch
+  void* dbuf2 = nullptr;
+  float* x_dev = nullptr;      // rank 0 input staging (f32 [B, w0])
+  float* t_dev = nullptr;      // last rank targets or dy staging (f32 [B, wL])
+  float* part = nullptr;       // loss partials
+  float* loss_dev = nullptr;
+  float* loss_host = nullptr;  // pinned
+  cudaEvent_t ev_start = nullptr, ev_end = nullptr, ev_fwd_join = nullptr, ev_bwd_join = nullptr;
+  std::vector<cudaEvent_t> ev_fr, ev_fd, ev_br, ev_bd;
+  float last_ms = 0.0f;
+  bool aborted = false;
+
+  uint64_t win(uint64_t l) const { return widths[first + l]; }       // local layer l input width
+  uint64_t wout(uint64_t l) const { return widths[first + l + 1]; }  // local layer l output width
+  bool is_first() const { return rank == 0; }
+  bool is_last() const { return rank + 1 == world; }
+  cudaStream_t comp() const { return ctx->stream; }
+  size_t es() const { return train_mode ? 2 : 4; }
+};
+
+namespace {
+
+lc_status alloc(void** p, size_t bytes) {
+  cudaError_t e = cudaMalloc(p, bytes ? bytes : 16);
+  if (e != cudaSuccess) return cuda_fail(e, "pipeline cudaMalloc");
+  return LC_OK;
+}
+
+lc_status setup(lc_pipeline* p) {
+  const uint64_t mbs = p->cfg.microbatches, mb = p->cfg.microbatch;
+  p->B = mbs * mb;
+  CU(cudaStreamCreateWithFlags(&p->s_fwd, cudaStreamNonBlocking));
+  CU(cudaStreamCreateWithFlags(&p->s_bwd, cudaStreamNonBlocking));
+  CU(cudaEventCreate(&p->ev_start));
+  CU(cudaEventCreate(&p->ev_end));
+  CU(cudaEventCreateWithFlags(&p->ev_fwd_join, cudaEventDisableTiming));
+  CU(cudaEventCreateWithFlags(&p->ev_bwd_join, cudaEventDisableTiming));
+  for (auto* v : {&p->ev_fr, &p->ev_fd, &p->ev_br, &p->ev_bd}) {
+    v->resize(mbs);
+    for (auto& e : *v) CU(cudaEventCreateWithFlags(&e, cudaEventDisableTiming));
+  }
+  const size_t es = p->es();
+  lc_status st;
+  for (uint64_t l = 0; l < p->count; l++) {
+    const uint64_t n = p->win(l) * p->wout(l);
+    float* m = nullptr;
+    if ((st = alloc((void**)&m, n * 4))) return st;
+    CU(cudaMemset(m, 0, n * 4));
+    p->master.push_back(m);
+    if (p->train_mode) {
+      void* b = nullptr;
+      if ((st = alloc(&b, n * 2))) return st;
+      CU(cudaMemset(b, 0, n * 2));
+      p->wb.push_back(b);
+    }
+    if (!p->train_mode || p->cfg.lr == 0.0f) {
+      float* g = nullptr;
+      if ((st = alloc((void**)&g, n * 4))) return st;
+      CU(cudaMemset(g, 0, n * 4));
+      p->dw.push_back(g);
+    }
+  }
+  for (uint64_t l = 0; l <= p->count; l++) {
+    void* h = nullptr;
+    const uint64_t w = l < p->count ? p->win(l) : p->wout(p->count - 1);
+    if ((st = alloc(&h, p->B * w * es))) return st;
+    p->H.push_back(h);
+  }
+  for (uint64_t l = 0; l < p->count; l++) {
+    if (p->train_mode) {
+      void* d = nullptr;
+      if ((st = alloc(&d, p->B * p->wout(l) * 2))) return st;
+      p->dP.push_back(d);
+    } else {
+      float* q = nullptr;
+      if ((st = alloc((void**)&q, p->B * p->wout(l) * 4))) return st;
+      p->pre.push_back(q);
+    }
+  }
+  if (!p->is_first() && (st = alloc(&p->gsend, p->B * p->win(0) * es))) return st;
+  if (!p->train_mode) {
+    uint64_t maxw = 0;
+    for (uint64_t l = 0; l <= p->count; l++) maxw = std::max(maxw, p->widths[p->first + l]);
+    if ((st = alloc(&p->dbuf, mb * maxw * 4))) return st;
+    if ((st = alloc(&p->dbuf2, mb * maxw * 4))) return st;
+    if (!p->is_last()) {  // received gradients (f32 [B, wL_local])
+      void* g = nullptr;
+      if ((st = alloc(&g, p->B * p->wout(p->count - 1) * 4))) return st;
+      p->dP.push_back(g);
+    }
+  }
+  if (p->is_first() && (st = alloc((void**)&p->x_dev, p->B * p->widths[0] * 4))) return st;
+  if (p->is_last() && (st = alloc((void**)&p->t_dev, p->B * p->widths.back() * 4))) return st;
+  if ((st = alloc((void**)&p->part, sizeof(float) * kMseBlocks * mbs))) return st;
+  if ((st = alloc((void**)&p->loss_dev, sizeof(float)))) return st;
+  CU(cudaMallocHost(&p->loss_host, sizeof(float)));
+  return LC_OK;
+}
+
+// ---- training-mode building blocks ------------------------------------------------------------
+
+GemmProblem bf16_problem(uint64_t m, uint64_t n, uint64_t k) {
+  GemmProblem g;
+  g.m = m;
+  g.n = n;
+  g.k = k;
+  g.batch = 1;
+  g.in_dtype = LC_BF16;
+  g.c_dtype = LC_BF16;
+  g.reserve_sms = 4;  // room for the NCCL transfer kernels next to the persistent GEMM
+  return g;
+}
+
+// H[l+1][rows] = relu(H[l][rows] @ Wb_l)
+lc_status fwd_layer(lc_pipeline* p, uint64_t l, uint64_t row0, uint64_t rows) {
+  const uint64_t k = p->win(l), n = p->wout(l);
+  GemmProblem g = bf16_problem(rows, n, k);
+  g.a.data = p->H[l];
+  g.a.offset = row0 * k;
+  g.a.mn = rows;
+  g.a.k = k;
+  g.a.mn_stride = (int64_t)k;
+  g.a.k_stride = 1;
+  g.b.data = p->wb[l];  // [k][n] row-major: element (n, k) at k*n_cols + n
+  g.b.mn = n;
+  g.b.k = k;
+  g.b.mn_stride = 1;
+  g.b.k_stride = (int64_t)n;
+  g.c = p->H[l + 1];
+  g.c_offset = row0 * n;
+  g.c_m_stride = (int64_t)n;
+  g.c_n_stride = 1;
+  g.relu = 1;
+  return gemm_run(p->ctx, p->comp(), g, nullptr, false);
+}
+
+// out[rows] = (dP[l][rows] @ Wb_l^T) where H[l][rows] > 0
+lc_status dgrad_layer(lc_pipeline* p, uint64_t l, uint64_t row0, uint64_t rows, void* out) {
+  const uint64_t k = p->wout(l), n = p->win(l);
+  GemmProblem g = bf16_problem(rows, n, k);
+  g.a.data = p->dP[l];
+  g.a.offset = row0 * k;
+  g.a.mn = rows;
+  g.a.k = k;
+  g.a.mn_stride = (int64_t)k;
+  g.a.k_stride = 1;
+  g.b.data = p->wb[l];  // B[k=j][n=i] = W[i][j]: element (n=i, k=j) at i*k + j
+  g.b.mn = n;
+  g.b.k = k;
+  g.b.mn_stride = (int64_t)k;
+  g.b.k_stride = 1;
+  g.c = out;
+  g.c_offset = row0 * n;
+  g.c_m_stride = (int64_t)n;
+  g.c_n_stride = 1;
+  g.epi = 1;
+  g.aux = p->H[l];  // the layer's input, same [B, n] layout as the output
+  return gemm_run(p->ctx, p->comp(), g, nullptr, false);
+}
+
+// W_l -= lr * H[l]^T @ dP[l] (K = B), Wb_l = bf16(W_l); or dW_l = H[l]^T @ dP[l] when lr == 0
+lc_status wgrad_layer(lc_pipeline* p, uint64_t l) {
+  const uint64_t m = p->win(l), n = p->wout(l), k = p->B;
+  GemmProblem g = bf16_problem(m, n, k);
+  g.a.data = p->H[l];  // A[m=i][k=b] = H[b][i]
+  g.a.mn = m;
+  g.a.k = k;
+  g.a.mn_stride = 1;
+  g.a.k_stride = (int64_t)m;
+  g.b.data = p->dP[l];  // B[k=b][n=j] = dP[b][j]
+  g.b.mn = n;
+  g.b.k = k;
+  g.b.mn_stride = 1;
+  g.b.k_stride = (int64_t)n;
+  g.c_m_stride = (int64_t)n;
+  g.c_n_stride = 1;
+  if (p->cfg.lr != 0.0f) {
+    g.epi = 2;
+    g.aux = p->master[l];
+    g.aux2 = p->wb[l];
+    g.lr = p->cfg.lr;
+    g.c = p->master[l];  // unused by the SGD epilogue; keeps the pointer valid
+    g.c_dtype = LC_F32;
+  } else {
+    g.c = p->dw[l];
+    g.c_dtype = LC_F32;
+  }
+  return gemm_run(p->ctx, p->comp(), g, nullptr, false);
+}
+
+// ---- reference-mode building blocks (the reference's Backend call sequence) -------------------
+
+lc_status ref_forward(lc_pipeline* p, uint64_t l, uint64_t row0, uint64_t rows) {
+  const uint64_t k = p->win(l), n = p->wout(l);
+  lc_view x = matrix_view((float*)p->H[l] + row0 * k, LC_F32, rows, k, rows * k * 4);
+  lc_view w = matrix_view(p->master[l], LC_F32, k, n, k * n * 4);
+  lc_view pre = matrix_view(p->pre[l] + row0 * n, LC_F32, rows, n, rows * n * 4);
+  lc_view act = matrix_view((float*)p->H[l + 1] + row0 * n, LC_F32, rows, n, rows * n * 4);
+  lc_status st = lc_backend_gemm(p->ctx, p->comp(), &x, &w, &pre, 1.0f, 0.0f);
+  if (st) return st;
+  return p->cfg.activation == 0 ? lc_gelu(p->ctx, p->comp(), &pre, &act) : lc_relu(p->ctx, p->comp(), &pre, &act);
+}
+
+// g: incoming gradient (f32 [rows, n]); writes dx into `dx_out` (f32 [rows, k]) unless null.
+lc_status ref_backward(lc_pipeline* p, uint64_t l, uint64_t row0, uint64_t rows, const float* g, float* dx_out) {
+  const uint64_t k = p->win(l), n = p->wout(l);
+  lc_view pre = matrix_view(p->pre[l] + row0 * n, LC_F32, rows, n, rows * n * 4);
+  lc_view gv = matrix_view(const_cast<float*>(g), LC_F32, rows, n, rows * n * 4);
+  lc_view dpre = matrix_view(p->dbuf, LC_F32, rows, n, rows * n * 4);
+  lc_status st = p->cfg.activation == 0 ? lc_gelu_backward(p->ctx, p->comp(), &pre, &gv, &dpre)
+                                         : lc_relu_backward(p->ctx, p->comp(), &pre, &gv, &dpre);
+  if (st) return st;
+  // dW[k, n] += x^T [k, rows] @ dpre [rows, n]  (crates/pipeline/src/lib.rs:218, beta = 1)
+  lc_view xt{};
+  xt.data = (float*)p->H[l] + row0 * k;
+  xt.buffer_bytes = rows * k * 4;
+  xt.dtype = LC_F32;
+  xt.rank = 2;
+  xt.shape[0] = k;
+  xt.shape[1] = rows;
+  xt.strides[0] = 1;
+  xt.strides[1] = k;
+  lc_view dwv = matrix_view(p->dw[l], LC_F32, k, n, k * n * 4);
+  if ((st = lc_backend_gemm(p->ctx, p->comp(), &xt, &dpre, &dwv, 1.0f, 1.0f))) return st;
+  if (dx_out == nullptr) return LC_OK;
+  // dX[rows, k] = dpre [rows, n] @ W^T [n, k]  (:220)
+  lc_view wt{};
+  wt.data = p->master[l];
+  wt.buffer_bytes = k * n * 4;
+  wt.dtype = LC_F32;
+  wt.rank = 2;
+  wt.shape[0] = n;
+  wt.shape[1] = k;
+  wt.strides[0] = 1;
+  wt.strides[1] = n;
+  lc_view dx = matrix_view(dx_out, LC_F32, rows, k, rows * k * 4);
+  return lc_backend_gemm(p->ctx, p->comp(), &dpre, &wt, &dx, 1.0f, 0.0f);
+}
+
+lc_status wait_step(lc_pipeline* p) {
+  using clock = std::chrono::steady_clock;
+  const auto t0 = clock::now();
+  const int64_t limit_ms = p->cfg.timeout_ms > 0 ? p->cfg.timeout_ms : 60000;
+  for (;;) {
+    cudaError_t q = cudaEventQuery(p->ev_end);
+    if (q == cudaSuccess) break;
+    if (q != cudaErrorNotReady) return cuda_fail(q, "pipeline step");
+    for (ncclComm_t c : {p->comm_fwd, p->comm_bwd}) {
+      if (c == nullptr) continue;
+      ncclResult_t ar = ncclSuccess;
+      if (ncclCommGetAsyncError(c, &ar) == ncclSuccess && ar != ncclSuccess && ar != ncclInProgress) {
+        ncclCommAbort(p->comm_fwd);
+        ncclCommAbort(p->comm_bwd);
+        p->comm_fwd = p->comm_bwd = nullptr;
+        p->aborted = true;
+        return nccl_fail(ar, "peer transfer failed");
+      }
+    }
+    if (std::chrono::duration_cast<std::chrono::milliseconds>(clock::now() - t0).count() > limit_ms) {
+      if (p->comm_fwd) ncclCommAbort(p->comm_fwd);
+      if (p->comm_bwd) ncclCommAbort(p->comm_bwd);
+      p->comm_fwd = p->comm_bwd = nullptr;
+      p->aborted = true;
+      return fail(LC_ERR_TRANSPORT, "pipeline step did not finish within timeout_ms; a peer is gone");
+    }
+    std::this_thread::sleep_for(std::chrono::microseconds(20));
+  }
+  CU(cudaEventElapsedTime(&p->last_ms, p->ev_start, p->ev_end));
+  return lc_sync(p->ctx, nullptr);
+}
+
+}  // namespace
+
+extern "C" {
+
+lc_status lc_pipeline_unique_id(uint8_t id[LC_PIPELINE_ID_BYTES]) {
+  static_assert(sizeof(ncclUniqueId) == LC_PIPELINE_ID_BYTES, "NCCL unique id size");
+  ncclUniqueId u;
+  NC(ncclGetUniqueId(&u));
+  memcpy(id, &u, sizeof(u));
+  return LC_OK;
+}
+
+lc_status lc_pipeline_create(const lc_pipeline_config* cfg, const uint8_t id[LC_PIPELINE_ID_BYTES], int32_t rank,
+                             int32_t world, int32_t device, lc_pipeline** out) {
+  if (cfg == nullptr || out == nullptr) return fail(LC_ERR_INVALID_ARGUMENT, "null argument");
+  if (world < 1 || rank < 0 || rank >= world) return fail(LC_ERR_SCHEDULE, "rank outside the world");
+  if (cfg->microbatches == 0 || cfg->microbatch == 0) return fail(LC_ERR_SCHEDULE, "no microbatches");
+  const bool train = cfg->compute_dtype == LC_BF16;
+  if (!train && cfg->compute_dtype != LC_F32) return fail(LC_ERR_DTYPE, "compute dtype is f32 or bf16");
+  if (train && (cfg->activation != 1 || cfg->loss != 1))
+    return fail(LC_ERR_INVALID_ARGUMENT, "training mode is ReLU layers with the MSE loss");
+  if (!train && (cfg->loss != 0 || cfg->lr != 0.0f))
+    return fail(LC_ERR_INVALID_ARGUMENT, "reference mode takes dy from the caller and applies no optimizer");
+  std::vector<uint64_t> owners(cfg->layers);
+  lc_status st = lc_contiguous_placement(cfg->layers, (uint64_t)world, owners.data());
+  if (st) return st;
+  auto* p = new lc_pipeline();
+  p->cfg = *cfg;
+  p->rank = rank;
+  p->world = world;
+  p->device = device;
+  p->train_mode = train;
+  for (uint64_t l = 0; l <= cfg->layers; l++) p->widths.push_back(cfg->widths ? cfg->widths[l] : cfg->width);
+  p->cfg.widths = nullptr;
+  for (uint64_t l = 0; l < cfg->layers; l++)
+    if (owners[l] == (uint64_t)rank) {
+      if (p->count == 0) p->first = l;
+      p->count++;
+    }
+  if (train)
+    for (uint64_t w : p->widths)
+      if (w % 8 != 0) {
+        delete p;
+        return fail(LC_ERR_SHAPE, "training mode widths must be multiples of 8 (16-byte rows)");
+      }
+  if ((st = lc_context_create(device, &p->ctx))) {
+    delete p;
+    return st;
+  }
+  if ((st = setup(p))) {
+    lc_pipeline_destroy(p);
+    return st;
+  }
+  if (world > 1) {
+    if (id == nullptr) {
+      lc_pipeline_destroy(p);
+      return fail(LC_ERR_INVALID_ARGUMENT, "null communicator id");
+    }
+    ncclUniqueId u;
+    memcpy(&u, id, sizeof(u));
+    ncclResult_t r = ncclCommInitRank(&p->comm_fwd, world, u, rank);
+    if (r == ncclSuccess) r = ncclCommSplit(p->comm_fwd, 0, rank, &p->comm_bwd, nullptr);
+    if (r != ncclSuccess) {
+      lc_pipeline_destroy(p);
+      return nccl_fail(r, "communicator setup");
+    }
+  }
+  *out = p;
+  return LC_OK;
+}
+
+lc_status lc_pipeline_destroy(lc_pipeline* p) {
+  if (p == nullptr) return LC_OK;
+  if (p->ctx) {
+    cudaSetDevice(p->device);
+    cudaDeviceSynchronize();
+  }
+  if (p->comm_bwd) ncclCommDestroy(p->comm_bwd);
+  if (p->comm_fwd) ncclCommDestroy(p->comm_fwd);
+  for (auto* v : {&p->master, &p->dw, &p->pre})
+    for (float* q : *v) cudaFree(q);
+  for (auto* v : {&p->wb, &p->H, &p->dP})
+    for (void* q : *v) cudaFree(q);
+  for (void* q : {p->gsend, p->dbuf, p->dbuf2, (void*)p->x_dev, (void*)p->t_dev, (void*)p->part, (void*)p->loss_dev})
+    if (q) cudaFree(q);
+  if (p->loss_host) cudaFreeHost(p->loss_host);
+  for (auto* v : {&p->ev_fr, &p->ev_fd, &p->ev_br, &p->ev_bd})
+    for (auto e : *v) cudaEventDestroy(e);
+  for (auto e : {p->ev_start, p->ev_end, p->ev_fwd_join, p->ev_bwd_join})
+    if (e) cudaEventDestroy(e);
+  if (p->s_fwd) cudaStreamDestroy(p->s_fwd);
+  if (p->s_bwd) cudaStreamDestroy(p->s_bwd);
+  if (p->ctx) lc_context_destroy(p->ctx);
+  delete p;
+  return LC_OK;
+}
+
+lc_status lc_pipeline_local_layers(lc_pipeline* p, uint64_t* first, uint64_t* count) {
+  if (!p || !first || !count) return fail(LC_ERR_INVALID_ARGUMENT, "null argument");
+  *first = p->first;
+  *count = p->count;
+  return LC_OK;
+}
+
+lc_status lc_pipeline_set_weight(lc_pipeline* p, uint64_t index, const float* host_w) {
+  if (!p || !host_w || index >= p->count) return fail(LC_ERR_INVALID_ARGUMENT, "bad layer index");
+  cudaSetDevice(p->device);
+  const uint64_t n = p->win(index) * p->wout(index);
+  CU(cudaMemcpy(p->master[index], host_w, n * 4, cudaMemcpyHostToDevice));
+  if (p->train_mode) {
+    to_bf16_kernel<<<blocks_for(p->ctx, n), 256, 0, p->comp()>>>(p->master[index], (uint16_t*)p->wb[index], n);
+    record_launch(p->ctx, "pipeline_to_bf16");
+    CU(cudaStreamSynchronize(p->comp()));
+  }
+  return LC_OK;
+}
+
+lc_status lc_pipeline_init_weights(lc_pipeline* p, uint64_t seed, float stddev) {
+  if (!p) return fail(LC_ERR_INVALID_ARGUMENT, "null pipeline");
+  cudaSetDevice(p->device);
+  for (uint64_t l = 0; l < p->count; l++) {
+    const uint64_t n = p->win(l) * p->wout(l);
+    normal_init_kernel<<<blocks_for(p->ctx, n), 256, 0, p->comp()>>>(
+        p->master[l], p->train_mode ? (uint16_t*)p->wb[l] : nullptr, n, seed + p->first + l, stddev);
+    record_launch(p->ctx, "pipeline_init_weights");
+  }
+  CU(cudaStreamSynchronize(p->comp()));
+  return LC_OK;
+}
+
+lc_status lc_pipeline_get_weight(lc_pipeline* p, uint64_t index, float* host_w) {
+  if (!p || !host_w || index >= p->count) return fail(LC_ERR_INVALID_ARGUMENT, "bad layer index");
+  cudaSetDevice(p->device);
+  CU(cudaMemcpy(host_w, p->master[index], p->win(index) * p->wout(index) * 4, cudaMemcpyDeviceToHost));
+  return LC_OK;
+}
+
+lc_status lc_pipeline_get_grad(lc_pipeline* p, uint64_t index, float* host_dw) {
+  if (!p || !host_dw || index >= p->count) return fail(LC_ERR_INVALID_ARGUMENT, "bad layer index");
+  if (p->dw.empty())
+    return fail(LC_ERR_INVALID_ARGUMENT, "the gradient is fused into the SGD update (lr != 0); nothing to read");
+  cudaSetDevice(p->device);
+  CU(cudaMemcpy(host_dw, p->dw[index], p->win(index) * p->wout(index) * 4, cudaMemcpyDeviceToHost));
+  return LC_OK;
+}
+
+lc_status lc_pipeline_get_output(lc_pipeline* p, float* host_y) {
+  if (!p || !host_y) return fail(LC_ERR_INVALID_ARGUMENT, "null argument");
+  if (!p->is_last()) return fail(LC_ERR_SCHEDULE, "only the last stage holds the output");
+  cudaSetDevice(p->device);
+  const uint64_t n = p->B * p->widths.back();
+  if (!p->train_mode) {
+    CU(cudaMemcpy(host_y, p->H[p->count], n * 4, cudaMemcpyDeviceToHost));
+    return LC_OK;
+  }
+  std::vector<uint16_t> h(n);
+  CU(cudaMemcpy(h.data(), p->H[p->count], n * 2, cudaMemcpyDeviceToHost));
+  for (uint64_t i = 0; i < n; i++) {
+    uint32_t b = ((uint32_t)h[i]) << 16;
+    memcpy(&host_y[i], &b, 4);
+  }
+  return LC_OK;
+}
+
+lc_status lc_pipeline_last_step_ms(lc_pipeline* p, float* ms) {
+  if (!p || !ms) return fail(LC_ERR_INVALID_ARGUMENT, "null argument");
+  *ms = p->last_ms;
+  return LC_OK;
+}
+
+void* lc_pipeline_stream(lc_pipeline* p) { return p ? p->comp() : nullptr; }
+
+uint64_t lc_pipeline_debug_launches(lc_pipeline* p) { return p ? lc_debug_launches(p->ctx) : 0; }
+
+lc_status lc_pipeline_step(lc_pipeline* p, const float* x, const float* target_or_dy, int32_t inputs_on_device,
+                           float* loss) {
+  if (!p) return fail(LC_ERR_INVALID_ARGUMENT, "null pipeline");
+  if (p->aborted) return fail(LC_ERR_TRANSPORT, "the pipeline's communicators were aborted");
+  if (p->is_first() && x == nullptr) return fail(LC_ERR_INVALID_ARGUMENT, "rank 0 needs the inputs");
+  if (p->is_last() && target_or_dy == nullptr) return fail(LC_ERR_INVALID_ARGUMENT, "the last rank needs targets or dy");
+  cudaSetDevice(p->device);
+  const uint64_t mbs = p->cfg.microbatches, mb = p->cfg.microbatch;
+  std::vector<int64_t> order(2 * mbs);
+  uint64_t n_ops = 0;
+  lc_status st = lc_local_order((uint64_t)p->world, (uint64_t)p->rank, mbs, order.data(), order.size(), &n_ops);
+  if (st) return st;
+  cudaStream_t cs = p->comp();
+  const ncclDataType_t nt = p->train_mode ? ncclBfloat16 : ncclFloat32;
+  const uint64_t w0 = p->win(0), wl = p->wout(p->count - 1);
+  const size_t es = p->es();
+  CU(cudaEventRecord(p->ev_start, cs));
+  // fork the transfer streams from the step start
+  CU(cudaStreamWaitEvent(p->s_fwd, p->ev_start, 0));
+  CU(cudaStreamWaitEvent(p->s_bwd, p->ev_start, 0));
+  const cudaMemcpyKind kind = inputs_on_device ? cudaMemcpyDeviceToDevice : cudaMemcpyHostToDevice;
+  if (p->is_first()) CU(cudaMemcpyAsync(p->x_dev, x, p->B * p->widths[0] * 4, kind, cs));
+  if (p->is_last()) CU(cudaMemcpyAsync(p->t_dev, target_or_dy, p->B * p->widths.back() * 4, kind, cs));
+  const float n_total = (float)(p->B * p->widths.back());
+
+  for (uint64_t i = 0; i < n_ops && !st; i++) {
+    const bool fwd = order[i] > 0;
+    const uint64_t m = (uint64_t)(fwd ? order[i] : -order[i]) - 1;
+    const uint64_t row0 = m * mb;
+    if (fwd) {
+      void* in = (uint8_t*)p->H[0] + row0 * w0 * es;
+      if (p->is_first()) {
+        if (p->train_mode) {
+          to_bf16_kernel<<<blocks_for(p->ctx, mb * w0), 256, 0, cs>>>(p->x_dev + row0 * w0, (uint16_t*)in, mb * w0);
+          record_launch(p->ctx, "pipeline_input_to_bf16");
+        } else {
+          CU(cudaMemcpyAsync(in, p->x_dev + row0 * w0, mb * w0 * 4, cudaMemcpyDeviceToDevice, cs));
+        }
+      } else {
+        NC(ncclRecv(in, mb * w0, nt, p->rank - 1, p->comm_fwd, p->s_fwd));
+        CU(cudaEventRecord(p->ev_fr[m], p->s_fwd));
+        CU(cudaStreamWaitEvent(cs, p->ev_fr[m], 0));
+      }
+      for (uint64_t l = 0; l < p->count && !st; l++)
+        st = p->train_mode ? fwd_layer(p, l, row0, mb) : ref_forward(p, l, row0, mb);
+      if (st) break;
+      void* outp = (uint8_t*)p->H[p->count] + row0 * wl * es;
+      if (!p->is_last()) {
+        CU(cudaEventRecord(p->ev_fd[m], cs));
+        CU(cudaStreamWaitEvent(p->s_fwd, p->ev_fd[m], 0));
+        NC(ncclSend(outp, mb * wl, nt, p->rank + 1, p->comm_fwd, p->s_fwd));
+      } else if (p->train_mode) {
+        mse_relu_kernel<<<kMseBlocks, kMseThreads, 0, cs>>>((const uint16_t*)outp, p->t_dev + row0 * wl,
+                                                          (uint16_t*)p->dP[p->count - 1] + row0 * wl, mb * wl, n_total,
+                                                          p->part + m * kMseBlocks);
+        record_launch(p->ctx, "pipeline_mse_relu");
+      }
+    } else {
+      // incoming gradient for the stage's last layer
+      const float* g_ref = nullptr;
+      if (!p->is_last()) {
+        void* gin = (uint8_t*)p->dP[p->train_mode ? p->count - 1 : 0] + row0 * wl * es;
+        NC(ncclRecv(gin, mb * wl, nt, p->rank + 1, p->comm_bwd, p->s_bwd));
+        CU(cudaEventRecord(p->ev_br[m], p->s_bwd));
+        CU(cudaStreamWaitEvent(cs, p->ev_br[m], 0));
+        g_ref = (const float*)gin;
+      } else {
+        g_ref = p->t_dev + row0 * wl;  // reference mode: dy
+      }
+      if (p->train_mode) {
+        for (uint64_t l = p->count; l-- > 0 && !st;) {
+          if (l > 0) st = dgrad_layer(p, l, row0, mb, p->dP[l - 1]);
+          else if (!p->is_first()) st = dgrad_layer(p, 0, row0, mb, p->gsend);
+        }
+      } else {
+        // g is consumed by the activation backward (into dbuf) before the dgrad GEMM writes dx,
+        // so dx can land in the buffer g came from (dbuf2) without any op reading and writing
+        // the same memory.
+        const float* g = g_ref;
+        for (uint64_t l = p->count; l-- > 0 && !st;) {
+          float* dx = nullptr;
+          if (l > 0) dx = (float*)p->dbuf2;
+          else if (!p->is_first()) dx = (float*)p->gsend + row0 * w0;
+          st = ref_backward(p, l, row0, mb, g, dx);
+          g = dx;
+        }
+      }
+      if (st) break;
+      if (!p->is_first()) {
+        CU(cudaEventRecord(p->ev_bd[m], cs));
+        CU(cudaStreamWaitEvent(p->s_bwd, p->ev_bd[m], 0));
+        NC(ncclSend((uint8_t*)p->gsend + row0 * w0 * es, mb * w0, nt, p->rank - 1, p->comm_bwd, p->s_bwd));
+      }
+    }
+  }
+  if (!st && p->train_mode)
+    for (uint64_t l = 0; l < p->count && !st; l++) st = wgrad_layer(p, l);
+  if (!st && p->train_mode && p->is_last()) {
+    loss_reduce_kernel<<<1, kMseThreads, 0, cs>>>(p->part, (int)(kMseBlocks * mbs), n_total, p->loss_dev);
+    record_launch(p->ctx, "pipeline_loss_reduce");
+    CU(cudaMemcpyAsync(p->loss_host, p->loss_dev, sizeof(float), cudaMemcpyDeviceToHost, cs));
+  }
+  // join the transfer streams before the step-end event
+  CU(cudaEventRecord(p->ev_fwd_join, p->s_fwd));
+  CU(cudaEventRecord(p->ev_bwd_join, p->s_bwd));
+  CU(cudaStreamWaitEvent(cs, p->ev_fwd_join, 0));
+  CU(cudaStreamWaitEvent(cs, p->ev_bwd_join, 0));
+  CU(cudaEventRecord(p->ev_end, cs));
+  lc_status wst = wait_step(p);
+  if (st) return st;
+  if (wst) return wst;
+  if (loss) *loss = (p->train_mode && p->is_last()) ? *p->loss_host : 0.0f;
+  return LC_OK;
+}
+
+}  // extern "C"

@@ -1,0 +1,108 @@
+"""GPU parity of the 1F1B pipeline against the CPU oracle (one stage on one GPU here; the
+multi-GPU runs use tests/test_pipeline_multigpu.py under several GPUs)."""
+import json
+from pathlib import Path
+
+import numpy as np
+import pytest
+
+import linalg_b200 as lb
+from linalg_b200 import data
+from linalg_b200.pipeline import Pipeline
+from oracle import oracle as O
+
+pytestmark = pytest.mark.gpu
+
+G = json.loads((Path(__file__).parent / "golden" / "reference_goldens.json").read_text())
+
+
+def fixture():
+    fx = G["pipeline_fixture"]
+    widths = fx["widths"]
+    ws = []
+    for l in range(len(widths) - 1):
+        w = np.zeros((widths[l], widths[l + 1]), np.float32)
+        for r in range(widths[l]):
+            for c in range(widths[l + 1]):
+                v = np.float32(np.float32(0.1) * np.float32(r + 1)) - np.float32(np.float32(0.05) * np.float32(c + 1))
+                w[r, c] = np.float32(v + np.float32(np.float32(0.02) * np.float32(l)))
+        ws.append(w)
+    return fx, widths, ws
+
+
+@pytest.mark.parametrize("act", ["gelu", "relu"])
+def test_reference_mode_tiny_fixture(gpu, act):
+    """crates/pipeline/tests/pipeline.rs fixture: y and dW of `train` on one stage."""
+    fx, widths, ws = fixture()
+    b = fx["batch"]
+    xs = np.stack([np.float32(fx["x0"]), np.float32(fx["x1"])]).reshape(2 * b, widths[0])
+    dys = np.stack([np.float32(fx["dy0"]), np.float32(fx["dy1"])]).reshape(2 * b, widths[-1])
+    p = Pipeline(3, 0, b, 2, activation=act, dtype="f32", lr=0.0, loss="dy", widths=widths)
+    for l, w in enumerate(ws):
+        p.set_weight(l, w)
+    p.step(xs, dys)
+    y = p.output()
+    ry, rdw = O.train_reference(act, widths, b, ws, [xs[:b], xs[b:]], [dys[:b], dys[b:]])
+    assert np.abs(y - ry.reshape(y.shape)).max() <= 1e-5
+    for l in range(3):
+        assert np.abs(p.get_grad(l) - rdw[l]).max() <= 1e-5 * max(1.0, np.abs(rdw[l]).max())
+    p.close()
+
+
+def test_reference_mode_wider_layers(gpu):
+    widths = [96, 160, 64, 128]
+    b, mbs = 8, 4
+    ws = [data.normal(10 + l, (widths[l], widths[l + 1]), scale=widths[l] ** -0.5) for l in range(3)]
+    xs = data.normal(1, (mbs * b, widths[0]))
+    dys = data.normal(2, (mbs * b, widths[-1]))
+    p = Pipeline(3, 0, b, mbs, activation="gelu", dtype="f32", lr=0.0, loss="dy", widths=widths)
+    for l, w in enumerate(ws):
+        p.set_weight(l, w)
+    p.step(xs, dys)
+    ry, rdw = O.train_reference("gelu", widths, b, ws, np.split(xs, mbs), np.split(dys, mbs))
+    y = p.output()
+    assert np.abs(y - ry.reshape(y.shape)).max() <= 1e-5 * np.abs(ry).max()
+    for l in range(3):
+        g = p.get_grad(l)
+        assert np.abs(g - rdw[l]).max() <= 1e-5 * np.abs(rdw[l]).max(), l
+    p.close()
+
+
+def test_training_step_matches_oracle_reduced_config(gpu):
+    """The benchmark step on a reduced config (d=256, L=4, 8 microbatches of 16): loss within
+    1e-2 relative of the CPU oracle, and the updated master weights close to the oracle's."""
+    L, d, mbs, mb, lr = 4, 256, 8, 16, 1e-1
+    B = mbs * mb
+    master = np.stack([data.normal(100 + l, (d, d), scale=d ** -0.5) for l in range(L)])
+    x = data.normal(1, (B, d))
+    t = data.normal(2, (B, d))
+    p = Pipeline(L, d, mb, mbs, lr=lr)
+    for l in range(L):
+        p.set_weight(l, master[l])
+    ref = master.copy()
+    losses, ref_losses = [], []
+    for step in range(3):
+        losses.append(p.step(x, t))
+        ref_losses.append(O.mlp_step(ref, x, t, mb, lr, threads=8))
+    for got, want in zip(losses, ref_losses):
+        assert abs(got - want) <= 1e-2 * abs(want), (losses, ref_losses)
+    assert losses[-1] < losses[0]
+    for l in range(L):
+        w = p.get_weight(l)
+        # the update itself (W after - W before) agrees within 5% of its size
+        assert np.abs(w - ref[l]).max() <= 5e-2 * np.abs(ref[l] - master[l]).max() + 1e-7
+    p.close()
+
+
+def test_training_step_is_deterministic(gpu):
+    L, d, mbs, mb = 2, 512, 4, 64
+    outs = []
+    for _ in range(2):
+        p = Pipeline(L, d, mb, mbs, lr=1e-3)
+        p.init_weights(7, d ** -0.5)
+        x = data.normal(1, (mbs * mb, d))
+        t = data.normal(2, (mbs * mb, d))
+        loss = p.step(x, t)
+        outs.append((loss, p.get_weight(0).tobytes(), p.get_weight(1).tobytes()))
+        p.close()
+    assert outs[0] == outs[1]
