@@ -274,6 +274,38 @@ def forward_gemm_roofline(hbm_peak):
             "algorithmic_bytes_per_launch": algo_bytes, "ms_per_launch": ms}
 
 
+def run_profile(args):
+    """Minimal drivers for ncu: no extras, no CPU work, a known number of launches."""
+    import torch
+    import linalg_b200 as lb
+    from linalg_b200 import data
+    from linalg_b200.pipeline import Pipeline
+
+    torch.cuda.set_device(0)
+    if args.profile == "gemm":
+        ctx = lb.Context(0)
+        ws = [torch.randn(WIDTH, WIDTH, device="cuda").bfloat16() for _ in range(4)]
+        x = torch.randn(MB, WIDTH, device="cuda").bfloat16()
+        y = torch.empty(MB, WIDTH, device="cuda", dtype=torch.bfloat16)
+        for i in range(args.steps):
+            lb.encode_gemm(ctx, None, 1.0, x, ws[i % 4], 0.0, y)
+        ctx.sync()
+        print(json.dumps({"profile": "gemm", "launches": ctx.debug_launches()[-8:]}))
+        return 0
+    p = Pipeline(LAYERS, WIDTH, MB, MBS, lr=LR)
+    p.init_weights(1234, WIDTH ** -0.5)
+    x = torch.from_numpy(data.normal(1, (BATCH, WIDTH))).cuda()
+    t = torch.from_numpy(data.normal(2, (BATCH, WIDTH))).cuda()
+    torch.cuda.synchronize()
+    n0 = p.debug_launches()
+    for _ in range(args.warmup + args.steps):
+        loss = p.step(x, t, on_device=True)
+    print(json.dumps({"profile": "step", "launches_per_step": (p.debug_launches() - n0) // (args.warmup + args.steps),
+                      "init_launches": n0, "loss": loss, "last_step_ms": p.last_step_ms}))
+    p.close()
+    return 0
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -281,9 +313,14 @@ def main():
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--no-extras", action="store_true", help="skip the N=1 contraction/op figures")
+    ap.add_argument("--profile", choices=["step", "gemm"], default=None,
+                    help="profiling driver: 'step' runs --warmup + --steps pipeline steps and nothing else; "
+                         "'gemm' runs --steps forward-shaped GEMMs ([64,8192] x [8192,8192] bf16)")
     args = ap.parse_args()
     if args.impl == "reference":
         return run_reference(args)
+    if args.profile is not None:
+        return run_profile(args)
 
     import numpy as np
     import torch

@@ -232,7 +232,8 @@ lc_status lc_context_create(int device, lc_context** out) {
     return cuda_fail(e, "cudaStreamCreate");
   }
   e = cudaMalloc(&ctx->d_error, sizeof(int));
-  if (e == cudaSuccess) e = cudaMemset(ctx->d_error, 0, sizeof(int));
+  if (e == cudaSuccess) e = cudaMemsetAsync(ctx->d_error, 0, sizeof(int), ctx->stream);
+  if (e == cudaSuccess) e = cudaStreamSynchronize(ctx->stream);
   if (e != cudaSuccess) {
     cudaStreamDestroy(ctx->stream);
     delete ctx;
@@ -265,10 +266,12 @@ lc_status lc_sync(lc_context* ctx, void* stream) {
   cudaError_t e = cudaStreamSynchronize(stream_of(ctx, stream));
   if (e != cudaSuccess) return cuda_fail(e, "cudaStreamSynchronize");
   int flag = 0;
-  e = cudaMemcpy(&flag, ctx->d_error, sizeof(int), cudaMemcpyDeviceToHost);
+  e = cudaMemcpyAsync(&flag, ctx->d_error, sizeof(int), cudaMemcpyDeviceToHost, ctx->stream);
+  if (e == cudaSuccess) e = cudaStreamSynchronize(ctx->stream);
   if (e != cudaSuccess) return cuda_fail(e, "reading the device error word");
   if (flag != 0) {
-    cudaMemset(ctx->d_error, 0, sizeof(int));
+    cudaMemsetAsync(ctx->d_error, 0, sizeof(int), ctx->stream);
+    cudaStreamSynchronize(ctx->stream);
     return fail(LC_ERR_DEVICE_TIMEOUT, "a kernel's bounded wait ran out; its output is not valid");
   }
   return LC_OK;

@@ -20,10 +20,12 @@
 // activation kernels and dW += x^T dpre per microbatch (beta = 1), exactly as `train` orders it.
 #include <cuda_bf16.h>
 #include <cuda_runtime.h>
+#include <dlfcn.h>
 #include <nccl.h>
 
 #include <chrono>
 #include <cstring>
+#include <mutex>
 #include <string>
 #include <thread>
 #include <vector>
@@ -34,6 +36,42 @@
 namespace {
 
 using namespace lc;
+
+// ---- NCCL, resolved at first use ---------------------------------------------------------------
+// The library does not link libnccl: a process that already loaded NCCL (torch does) keeps its
+// copy, and only a process without one loads libnccl.so.2 here.  Two copies of NCCL with the
+// same soname in one process would otherwise race for the symbols at load time.
+struct NcclApi {
+  ncclResult_t (*GetUniqueId)(ncclUniqueId*) = nullptr;
+  ncclResult_t (*CommInitRank)(ncclComm_t*, int, ncclUniqueId, int) = nullptr;
+  ncclResult_t (*CommSplit)(ncclComm_t, int, int, ncclComm_t*, ncclConfig_t*) = nullptr;
+  ncclResult_t (*CommDestroy)(ncclComm_t) = nullptr;
+  ncclResult_t (*CommAbort)(ncclComm_t) = nullptr;
+  ncclResult_t (*CommGetAsyncError)(ncclComm_t, ncclResult_t*) = nullptr;
+  ncclResult_t (*Send)(const void*, size_t, ncclDataType_t, int, ncclComm_t, cudaStream_t) = nullptr;
+  ncclResult_t (*Recv)(void*, size_t, ncclDataType_t, int, ncclComm_t, cudaStream_t) = nullptr;
+  const char* (*GetErrorString)(ncclResult_t) = nullptr;
+  bool ok = false;
+};
+
+const NcclApi& nccl() {
+  static NcclApi api;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    void* h = dlopen("libnccl.so.2", RTLD_NOW | RTLD_NOLOAD);
+    if (h == nullptr) h = dlopen("libnccl.so.2", RTLD_NOW | RTLD_LOCAL);
+    if (h == nullptr) return;
+    auto sym = [&](auto& fn, const char* name) {
+      fn = reinterpret_cast<std::remove_reference_t<decltype(fn)>>(dlsym(h, name));
+      return fn != nullptr;
+    };
+    api.ok = sym(api.GetUniqueId, "ncclGetUniqueId") && sym(api.CommInitRank, "ncclCommInitRank") &&
+             sym(api.CommSplit, "ncclCommSplit") && sym(api.CommDestroy, "ncclCommDestroy") &&
+             sym(api.CommAbort, "ncclCommAbort") && sym(api.CommGetAsyncError, "ncclCommGetAsyncError") &&
+             sym(api.Send, "ncclSend") && sym(api.Recv, "ncclRecv") && sym(api.GetErrorString, "ncclGetErrorString");
+  });
+  return api;
+}
 
 // ---- kernels ----------------------------------------------------------------------------------
 
@@ -120,7 +158,8 @@ unsigned blocks_for(lc_context* ctx, uint64_t n, unsigned per = 256) {
 // ---- helpers -----------------------------------------------------------------------------------
 
 lc_status nccl_fail(ncclResult_t r, const char* what) {
-  return fail(LC_ERR_TRANSPORT, std::string(what) + ": " + ncclGetErrorString(r));
+  const char* s = nccl().ok ? nccl().GetErrorString(r) : "NCCL unavailable";
+  return fail(LC_ERR_TRANSPORT, std::string(what) + ": " + s);
 }
 
 #define CU(x)                                          \
@@ -186,6 +225,15 @@ namespace {
 lc_status alloc(void** p, size_t bytes) {
   cudaError_t e = cudaMalloc(p, bytes ? bytes : 16);
   if (e != cudaSuccess) return cuda_fail(e, "pipeline cudaMalloc");
+  return LC_OK;
+}
+
+// Host <-> device copy ordered on the stage's own (non-blocking) stream and waited for.  A plain
+// cudaMemcpy runs on the legacy stream, which a non-blocking stream does not wait for, and from
+// pageable memory it may return before its DMA has landed.
+lc_status copy_sync(lc_pipeline* p, void* dst, const void* src, size_t bytes, cudaMemcpyKind kind) {
+  CU(cudaMemcpyAsync(dst, src, bytes, kind, p->comp()));
+  CU(cudaStreamSynchronize(p->comp()));
   return LC_OK;
 }
 
@@ -257,6 +305,8 @@ lc_status setup(lc_pipeline* p) {
   if ((st = alloc((void**)&p->part, sizeof(float) * kMseBlocks * mbs))) return st;
   if ((st = alloc((void**)&p->loss_dev, sizeof(float)))) return st;
   CU(cudaMallocHost(&p->loss_host, sizeof(float)));
+  // the zero fills above ran on the legacy stream; finish them before the stage stream runs
+  CU(cudaDeviceSynchronize());
   return LC_OK;
 }
 
@@ -411,17 +461,17 @@ lc_status wait_step(lc_pipeline* p) {
     for (ncclComm_t c : {p->comm_fwd, p->comm_bwd}) {
       if (c == nullptr) continue;
       ncclResult_t ar = ncclSuccess;
-      if (ncclCommGetAsyncError(c, &ar) == ncclSuccess && ar != ncclSuccess && ar != ncclInProgress) {
-        ncclCommAbort(p->comm_fwd);
-        ncclCommAbort(p->comm_bwd);
+      if (nccl().CommGetAsyncError(c, &ar) == ncclSuccess && ar != ncclSuccess && ar != ncclInProgress) {
+        nccl().CommAbort(p->comm_fwd);
+        nccl().CommAbort(p->comm_bwd);
         p->comm_fwd = p->comm_bwd = nullptr;
         p->aborted = true;
         return nccl_fail(ar, "peer transfer failed");
       }
     }
     if (std::chrono::duration_cast<std::chrono::milliseconds>(clock::now() - t0).count() > limit_ms) {
-      if (p->comm_fwd) ncclCommAbort(p->comm_fwd);
-      if (p->comm_bwd) ncclCommAbort(p->comm_bwd);
+      if (p->comm_fwd) nccl().CommAbort(p->comm_fwd);
+      if (p->comm_bwd) nccl().CommAbort(p->comm_bwd);
       p->comm_fwd = p->comm_bwd = nullptr;
       p->aborted = true;
       return fail(LC_ERR_TRANSPORT, "pipeline step did not finish within timeout_ms; a peer is gone");
@@ -438,8 +488,9 @@ extern "C" {
 
 lc_status lc_pipeline_unique_id(uint8_t id[LC_PIPELINE_ID_BYTES]) {
   static_assert(sizeof(ncclUniqueId) == LC_PIPELINE_ID_BYTES, "NCCL unique id size");
+  if (!nccl().ok) return fail(LC_ERR_TRANSPORT, "libnccl.so.2 could not be loaded");
   ncclUniqueId u;
-  NC(ncclGetUniqueId(&u));
+  NC(nccl().GetUniqueId(&u));
   memcpy(id, &u, sizeof(u));
   return LC_OK;
 }
@@ -492,8 +543,12 @@ lc_status lc_pipeline_create(const lc_pipeline_config* cfg, const uint8_t id[LC_
     }
     ncclUniqueId u;
     memcpy(&u, id, sizeof(u));
-    ncclResult_t r = ncclCommInitRank(&p->comm_fwd, world, u, rank);
-    if (r == ncclSuccess) r = ncclCommSplit(p->comm_fwd, 0, rank, &p->comm_bwd, nullptr);
+    if (!nccl().ok) {
+      lc_pipeline_destroy(p);
+      return fail(LC_ERR_TRANSPORT, "libnccl.so.2 could not be loaded");
+    }
+    ncclResult_t r = nccl().CommInitRank(&p->comm_fwd, world, u, rank);
+    if (r == ncclSuccess) r = nccl().CommSplit(p->comm_fwd, 0, rank, &p->comm_bwd, nullptr);
     if (r != ncclSuccess) {
       lc_pipeline_destroy(p);
       return nccl_fail(r, "communicator setup");
@@ -509,8 +564,8 @@ lc_status lc_pipeline_destroy(lc_pipeline* p) {
     cudaSetDevice(p->device);
     cudaDeviceSynchronize();
   }
-  if (p->comm_bwd) ncclCommDestroy(p->comm_bwd);
-  if (p->comm_fwd) ncclCommDestroy(p->comm_fwd);
+  if (p->comm_bwd) nccl().CommDestroy(p->comm_bwd);
+  if (p->comm_fwd) nccl().CommDestroy(p->comm_fwd);
   for (auto* v : {&p->master, &p->dw, &p->pre})
     for (float* q : *v) cudaFree(q);
   for (auto* v : {&p->wb, &p->H, &p->dP})
@@ -540,7 +595,8 @@ lc_status lc_pipeline_set_weight(lc_pipeline* p, uint64_t index, const float* ho
   if (!p || !host_w || index >= p->count) return fail(LC_ERR_INVALID_ARGUMENT, "bad layer index");
   cudaSetDevice(p->device);
   const uint64_t n = p->win(index) * p->wout(index);
-  CU(cudaMemcpy(p->master[index], host_w, n * 4, cudaMemcpyHostToDevice));
+  lc_status st = copy_sync(p, p->master[index], host_w, n * 4, cudaMemcpyHostToDevice);
+  if (st) return st;
   if (p->train_mode) {
     to_bf16_kernel<<<blocks_for(p->ctx, n), 256, 0, p->comp()>>>(p->master[index], (uint16_t*)p->wb[index], n);
     record_launch(p->ctx, "pipeline_to_bf16");
@@ -565,8 +621,7 @@ lc_status lc_pipeline_init_weights(lc_pipeline* p, uint64_t seed, float stddev) 
 lc_status lc_pipeline_get_weight(lc_pipeline* p, uint64_t index, float* host_w) {
   if (!p || !host_w || index >= p->count) return fail(LC_ERR_INVALID_ARGUMENT, "bad layer index");
   cudaSetDevice(p->device);
-  CU(cudaMemcpy(host_w, p->master[index], p->win(index) * p->wout(index) * 4, cudaMemcpyDeviceToHost));
-  return LC_OK;
+  return copy_sync(p, host_w, p->master[index], p->win(index) * p->wout(index) * 4, cudaMemcpyDeviceToHost);
 }
 
 lc_status lc_pipeline_get_grad(lc_pipeline* p, uint64_t index, float* host_dw) {
@@ -574,8 +629,7 @@ lc_status lc_pipeline_get_grad(lc_pipeline* p, uint64_t index, float* host_dw) {
   if (p->dw.empty())
     return fail(LC_ERR_INVALID_ARGUMENT, "the gradient is fused into the SGD update (lr != 0); nothing to read");
   cudaSetDevice(p->device);
-  CU(cudaMemcpy(host_dw, p->dw[index], p->win(index) * p->wout(index) * 4, cudaMemcpyDeviceToHost));
-  return LC_OK;
+  return copy_sync(p, host_dw, p->dw[index], p->win(index) * p->wout(index) * 4, cudaMemcpyDeviceToHost);
 }
 
 lc_status lc_pipeline_get_output(lc_pipeline* p, float* host_y) {
@@ -583,12 +637,10 @@ lc_status lc_pipeline_get_output(lc_pipeline* p, float* host_y) {
   if (!p->is_last()) return fail(LC_ERR_SCHEDULE, "only the last stage holds the output");
   cudaSetDevice(p->device);
   const uint64_t n = p->B * p->widths.back();
-  if (!p->train_mode) {
-    CU(cudaMemcpy(host_y, p->H[p->count], n * 4, cudaMemcpyDeviceToHost));
-    return LC_OK;
-  }
+  if (!p->train_mode) return copy_sync(p, host_y, p->H[p->count], n * 4, cudaMemcpyDeviceToHost);
   std::vector<uint16_t> h(n);
-  CU(cudaMemcpy(h.data(), p->H[p->count], n * 2, cudaMemcpyDeviceToHost));
+  lc_status st = copy_sync(p, h.data(), p->H[p->count], n * 2, cudaMemcpyDeviceToHost);
+  if (st) return st;
   for (uint64_t i = 0; i < n; i++) {
     uint32_t b = ((uint32_t)h[i]) << 16;
     memcpy(&host_y[i], &b, 4);
@@ -645,7 +697,7 @@ lc_status lc_pipeline_step(lc_pipeline* p, const float* x, const float* target_o
           CU(cudaMemcpyAsync(in, p->x_dev + row0 * w0, mb * w0 * 4, cudaMemcpyDeviceToDevice, cs));
         }
       } else {
-        NC(ncclRecv(in, mb * w0, nt, p->rank - 1, p->comm_fwd, p->s_fwd));
+        NC(nccl().Recv(in, mb * w0, nt, p->rank - 1, p->comm_fwd, p->s_fwd));
         CU(cudaEventRecord(p->ev_fr[m], p->s_fwd));
         CU(cudaStreamWaitEvent(cs, p->ev_fr[m], 0));
       }
@@ -656,7 +708,7 @@ lc_status lc_pipeline_step(lc_pipeline* p, const float* x, const float* target_o
       if (!p->is_last()) {
         CU(cudaEventRecord(p->ev_fd[m], cs));
         CU(cudaStreamWaitEvent(p->s_fwd, p->ev_fd[m], 0));
-        NC(ncclSend(outp, mb * wl, nt, p->rank + 1, p->comm_fwd, p->s_fwd));
+        NC(nccl().Send(outp, mb * wl, nt, p->rank + 1, p->comm_fwd, p->s_fwd));
       } else if (p->train_mode) {
         mse_relu_kernel<<<kMseBlocks, kMseThreads, 0, cs>>>((const uint16_t*)outp, p->t_dev + row0 * wl,
                                                           (uint16_t*)p->dP[p->count - 1] + row0 * wl, mb * wl, n_total,
@@ -668,7 +720,7 @@ lc_status lc_pipeline_step(lc_pipeline* p, const float* x, const float* target_o
       const float* g_ref = nullptr;
       if (!p->is_last()) {
         void* gin = (uint8_t*)p->dP[p->train_mode ? p->count - 1 : 0] + row0 * wl * es;
-        NC(ncclRecv(gin, mb * wl, nt, p->rank + 1, p->comm_bwd, p->s_bwd));
+        NC(nccl().Recv(gin, mb * wl, nt, p->rank + 1, p->comm_bwd, p->s_bwd));
         CU(cudaEventRecord(p->ev_br[m], p->s_bwd));
         CU(cudaStreamWaitEvent(cs, p->ev_br[m], 0));
         g_ref = (const float*)gin;
@@ -697,7 +749,7 @@ lc_status lc_pipeline_step(lc_pipeline* p, const float* x, const float* target_o
       if (!p->is_first()) {
         CU(cudaEventRecord(p->ev_bd[m], cs));
         CU(cudaStreamWaitEvent(p->s_bwd, p->ev_bd[m], 0));
-        NC(ncclSend((uint8_t*)p->gsend + row0 * w0 * es, mb * w0, nt, p->rank - 1, p->comm_bwd, p->s_bwd));
+        NC(nccl().Send((uint8_t*)p->gsend + row0 * w0 * es, mb * w0, nt, p->rank - 1, p->comm_bwd, p->s_bwd));
       }
     }
   }

@@ -72,7 +72,8 @@ class lc_contract_plan(C.Structure):
 
 
 class lc_pipeline_config(C.Structure):
-    _fields_ = [("layers", C.c_uint64), ("width", C.c_uint64), ("microbatch", C.c_uint64),
+    _fields_ = [("layers", C.c_uint64), ("width", C.c_uint64), ("widths", C.POINTER(C.c_uint64)),
+                ("microbatch", C.c_uint64),
                 ("microbatches", C.c_uint64), ("activation", C.c_int32), ("compute_dtype", C.c_int32),
                 ("lr", C.c_float), ("loss", C.c_int32), ("timeout_ms", C.c_int32)]
 
