@@ -253,6 +253,8 @@ lc_status lc_context_destroy(lc_context* ctx) {
   if (ctx == nullptr) return LC_OK;
   cudaSetDevice(ctx->device);
   cudaStreamSynchronize(ctx->stream);
+  if (ctx->split_part) cudaFree(ctx->split_part);
+  if (ctx->split_cnt) cudaFree(ctx->split_cnt);
   cudaFree(ctx->d_error);
   cudaStreamDestroy(ctx->stream);
   delete ctx;
@@ -271,6 +273,8 @@ lc_status lc_sync(lc_context* ctx, void* stream) {
   if (e != cudaSuccess) return cuda_fail(e, "reading the device error word");
   if (flag != 0) {
     cudaMemsetAsync(ctx->d_error, 0, sizeof(int), ctx->stream);
+    // a launch that gave up may have left split-K arrival counters raised
+    if (ctx->split_cnt) cudaMemsetAsync(ctx->split_cnt, 0, ctx->split_cnt_n * sizeof(int), ctx->stream);
     cudaStreamSynchronize(ctx->stream);
     return fail(LC_ERR_DEVICE_TIMEOUT, "a kernel's bounded wait ran out; its output is not valid");
   }

@@ -27,6 +27,7 @@
 #include <cstring>
 #include <mutex>
 #include <string>
+#include <unordered_map>
 
 #include "gemm.h"
 #include "internal.h"
@@ -45,14 +46,14 @@ struct KParams {
   uint32_t a_mn, b_mn;
   uint32_t idesc;
   // epilogue
-  int32_t mode;     // 0: C = alpha*acc + beta*C (+relu) ; 1: raw f32 partial
   int32_t c_dtype;  // LC_F32 / LC_BF16 / LC_F16
   int32_t relu;
-  int32_t vec_ok;   // C rows contiguous (c_ns == 1) and 16-byte aligned for every 32-column group
   void* c;
   int64_t c_off, c_bs, c_ms, c_ns;
   float alpha, beta;
-  float* partial;
+  float* partial;   // split-K: [splits][batch][M][N] raw partial sums
+  int* counters;    // split-K fixup: one arrival counter per (batch, tile, epilogue warp), zero at launch
+  int32_t fixup;    // 1: the last-arriving warp reduces in the kernel; 0: a separate reduce kernel does
   int* err;
   int32_t epi;       // 0 standard, 1 ReLU-mask by aux, 2 fused SGD into aux (f32) / aux2 (bf16)
   const void* aux;
@@ -70,14 +71,19 @@ struct Cfg {
   static constexpr int B_BYTES = BN * kRowBytes;
   static constexpr int STAGE_BYTES = (A_BYTES + B_BYTES) * (TF32X3 ? 2 : 1);
   static constexpr int STAGES = (TF32X3 ? 196608 : 196608) / STAGE_BYTES;
-  static constexpr int TMEM_COLS = 2 * BN < 32 ? 32 : 2 * BN;
+  // 2 accumulators (+ the 3xTF32 running sum), rounded up to the power of two tcgen05.alloc takes
+  static constexpr int TMEM_NEED = (TF32X3 ? 3 : 2) * BN;
+  static constexpr int TMEM_COLS = TMEM_NEED <= 32 ? 32 : TMEM_NEED <= 64 ? 64 : TMEM_NEED <= 128 ? 128
+                                   : TMEM_NEED <= 256 ? 256 : 512;
+  static_assert(TMEM_NEED <= 512, "TMEM holds 512 columns");
   static constexpr int THREADS = TF32X3 ? 320 : 192;
   // k-tiles per accumulator hand-off: one per unit for 16-bit inputs; 2 (64 K values, 24 MMAs)
   // for 3xTF32, which bounds the truncation bias of the tensor core's f32 accumulation to
   // about 24 ulp-halves per chunk while the chunks themselves are summed round-to-nearest.
   static constexpr int KC = TF32X3 ? 2 : (1 << 30);
   static constexpr int BAR_BYTES = 8 * (3 * STAGES + 5) + 16;
-  static constexpr int SMEM = STAGES * STAGE_BYTES + BAR_BYTES + 1024;
+  static constexpr int EPI_STAGE_BYTES = 4 * 32 * 33 * 4;  // one 32x33 f32 transpose tile per epilogue warp
+  static constexpr int SMEM = STAGES * STAGE_BYTES + ((BAR_BYTES + 15) / 16) * 16 + EPI_STAGE_BYTES + 1024;
   static_assert(STAGES >= 2, "at least two stages");
 };
 
@@ -147,86 +153,122 @@ __device__ __forceinline__ void apply_store(const KParams& p, int64_t idx, float
   }
 }
 
-// Epilogue for one 32-column group of one row held by this thread.
-__device__ __forceinline__ void epilogue_group(const KParams& p, const uint32_t (&r)[32], int32_t b, int32_t split,
-                                               int32_t m, int32_t n0) {
+__device__ __forceinline__ float* partial_row(const KParams& p, int32_t split, int32_t b, int32_t m) {
+  return p.partial + (((int64_t)split * p.batch + b) * p.M + m) * (int64_t)p.N;
+}
+
+// The epilogue of 32 elements at C indices i0 + j*st (bit j of `valid` set when element j exists).
+// Every value the epilogue reads (old C for beta, the ReLU mask, the SGD master weight) is loaded
+// for all 32 elements before the first store, so the loads are in flight together instead of each
+// waiting behind the previous element's store.
+__device__ __forceinline__ void apply32(const KParams& p, const float (&acc)[32], int64_t i0, int64_t st,
+                                        uint32_t valid) {
+  float old[32];
+  // pass 1: every read this epilogue needs, back to back
+  const bool reads = p.epi != 0 || p.beta != 0.0f;
+  if (reads) {
+    int64_t idx = i0;
+#pragma unroll
+    for (int j = 0; j < 32; j++, idx += st) {
+      float o = 0.0f;
+      if ((valid >> j) & 1u) {
+        if (p.epi == 0) o = load_c(p, idx);
+        else if (p.epi == 1) o = __uint_as_float(((uint32_t) static_cast<const uint16_t*>(p.aux)[idx]) << 16);
+        else o = static_cast<const float*>(p.aux)[idx];
+      }
+      old[j] = o;
+    }
+  }
+  // pass 2: compute and store
+  int64_t idx = i0;
+#pragma unroll
+  for (int j = 0; j < 32; j++, idx += st) {
+    if (!((valid >> j) & 1u)) continue;
+    if (p.epi == 0) {
+      store_c(p, idx, finish(p, acc[j], reads ? old[j] : 0.0f));
+    } else if (p.epi == 1) {
+      store_c(p, idx, old[j] > 0.0f ? __fmul_rn(p.alpha, acc[j]) : 0.0f);
+    } else {
+      const float w = __fsub_rn(old[j], __fmul_rn(p.lr, __fmul_rn(p.alpha, acc[j])));
+      static_cast<float*>(const_cast<void*>(p.aux))[idx] = w;
+      static_cast<uint16_t*>(p.aux2)[idx] = f32_to_bf16_rne(w);
+    }
+  }
+}
+
+// Output of one 32-column group [n0, n0 + 32) of the warp's 32 rows [m0, m0 + 32): lane l holds
+// row m0 + l in r[0..31].  When C's columns are contiguous (c_ns == 1), the group goes through the
+// warp's 32x33 shared tile so that every store instruction covers 32 consecutive columns of one
+// row (coalesced); otherwise (the swapped skinny products, whose rows are contiguous) each lane
+// stores its own row and consecutive lanes hit consecutive addresses.  `to_partial` writes the
+// raw accumulator into this split's partial row instead.
+__device__ __forceinline__ void store_group(const KParams& p, const uint32_t (&r)[32], int32_t b, int32_t m0, int32_t n0,
+                                            float* stage, bool to_partial, int32_t split) {
+  const int lane = threadIdx.x & 31;
+  if (to_partial || p.c_ns == 1) {
+#pragma unroll
+    for (int j = 0; j < 32; j++) stage[lane * 33 + j] = __uint_as_float(r[j]);
+    __syncwarp();
+    const int32_t n = n0 + lane;
+    float v[32];
+    uint32_t valid = 0;
+#pragma unroll
+    for (int i = 0; i < 32; i++) {
+      v[i] = stage[i * 33 + lane];
+      if (m0 + i < p.M && n < p.N) valid |= 1u << i;
+    }
+    __syncwarp();
+    if (to_partial) {
+      float* dst = partial_row(p, split, b, m0) + n;
+#pragma unroll
+      for (int i = 0; i < 32; i++)
+        if ((valid >> i) & 1u) dst[(int64_t)i * p.N] = v[i];
+    } else {
+      apply32(p, v, p.c_off + (int64_t)b * p.c_bs + (int64_t)m0 * p.c_ms + n, p.c_ms, valid);
+    }
+    return;
+  }
+  const int32_t m = m0 + lane;
   if (m >= p.M) return;
-  if (p.mode == 1) {
-    float* dst = p.partial + (((int64_t)split * p.batch + b) * p.M + m) * (int64_t)p.N + n0;
-    if (n0 + 32 <= p.N && (p.N % 4) == 0) {
-#pragma unroll
-      for (int j = 0; j < 32; j += 4)
-        *reinterpret_cast<float4*>(dst + j) = make_float4(__uint_as_float(r[j]), __uint_as_float(r[j + 1]),
-                                                          __uint_as_float(r[j + 2]), __uint_as_float(r[j + 3]));
-    } else {
-#pragma unroll
-      for (int j = 0; j < 32; j++)
-        if (n0 + j < p.N) dst[j] = __uint_as_float(r[j]);
-    }
-    return;
-  }
-  const int64_t base = p.c_off + (int64_t)b * p.c_bs + (int64_t)m * p.c_ms;
-  if (p.vec_ok && n0 + 32 <= p.N && p.epi == 2) {
-    // fused SGD: 16-byte master loads/stores and 16-byte bf16 stores
-    const int64_t at = base + (int64_t)n0;
-    float* master = static_cast<float*>(const_cast<void*>(p.aux)) + at;
-    uint16_t* wb = static_cast<uint16_t*>(p.aux2) + at;
-#pragma unroll
-    for (int j = 0; j < 32; j += 8) {
-      float4 w0 = *reinterpret_cast<const float4*>(master + j);
-      float4 w1 = *reinterpret_cast<const float4*>(master + j + 4);
-      float w[8] = {w0.x, w0.y, w0.z, w0.w, w1.x, w1.y, w1.z, w1.w};
-      uint4 out;
-      uint16_t* oo = reinterpret_cast<uint16_t*>(&out);
-#pragma unroll
-      for (int e = 0; e < 8; e++) {
-        w[e] = __fsub_rn(w[e], __fmul_rn(p.lr, __fmul_rn(p.alpha, __uint_as_float(r[j + e]))));
-        oo[e] = f32_to_bf16_rne(w[e]);
-      }
-      *reinterpret_cast<float4*>(master + j) = make_float4(w[0], w[1], w[2], w[3]);
-      *reinterpret_cast<float4*>(master + j + 4) = make_float4(w[4], w[5], w[6], w[7]);
-      *reinterpret_cast<uint4*>(wb + j) = out;
-    }
-    return;
-  }
-  if (p.vec_ok && n0 + 32 <= p.N && p.epi == 0) {
-    const int64_t at = base + (int64_t)n0;  // c_ns == 1
-    if (p.c_dtype == LC_F32) {
-      float* dst = static_cast<float*>(p.c) + at;
-#pragma unroll
-      for (int j = 0; j < 32; j += 4) {
-        float4 old = make_float4(0.f, 0.f, 0.f, 0.f);
-        if (p.beta != 0.0f) old = *reinterpret_cast<const float4*>(dst + j);
-        float4 v = make_float4(finish(p, __uint_as_float(r[j]), old.x), finish(p, __uint_as_float(r[j + 1]), old.y),
-                               finish(p, __uint_as_float(r[j + 2]), old.z), finish(p, __uint_as_float(r[j + 3]), old.w));
-        *reinterpret_cast<float4*>(dst + j) = v;
-      }
-    } else {
-      uint16_t* dst = static_cast<uint16_t*>(p.c) + at;
-#pragma unroll
-      for (int j = 0; j < 32; j += 8) {
-        uint4 old = make_uint4(0, 0, 0, 0);
-        if (p.beta != 0.0f) old = *reinterpret_cast<const uint4*>(dst + j);
-        const uint16_t* oh = reinterpret_cast<const uint16_t*>(&old);
-        uint4 out;
-        uint16_t* oo = reinterpret_cast<uint16_t*>(&out);
-#pragma unroll
-        for (int e = 0; e < 8; e++) {
-          float cold = p.c_dtype == LC_BF16 ? __uint_as_float(((uint32_t)oh[e]) << 16)
-                                            : __half2float(__ushort_as_half(oh[e]));
-          float v = finish(p, __uint_as_float(r[j + e]), cold);
-          oo[e] = p.c_dtype == LC_BF16 ? f32_to_bf16_rne(v) : __half_as_ushort(__float2half_rn(v));
-        }
-        *reinterpret_cast<uint4*>(dst + j) = out;
-      }
-    }
-    return;
-  }
+  float v[32];
+  uint32_t valid = 0;
 #pragma unroll
   for (int j = 0; j < 32; j++) {
-    const int32_t n = n0 + j;
-    if (n < p.N) apply_store(p, base + (int64_t)n * p.c_ns, __uint_as_float(r[j]));
+    v[j] = __uint_as_float(r[j]);
+    if (n0 + j < p.N) valid |= 1u << j;
   }
+  apply32(p, v, p.c_off + (int64_t)b * p.c_bs + (int64_t)m * p.c_ms + (int64_t)n0 * p.c_ns, p.c_ns, valid);
+}
+
+// Last CTA of a split tile: sum the splits' partial rows in split order and store the group.
+__device__ __forceinline__ void reduce_group(const KParams& p, int32_t b, int32_t m0, int32_t n0, float* stage) {
+  const int lane = threadIdx.x & 31;
+  uint32_t r[32];
+  const int32_t m = m0 + lane;
+  if (m < p.M && n0 + 32 <= p.N && (p.N % 4) == 0) {
+#pragma unroll
+    for (int j = 0; j < 32; j++) r[j] = 0u;
+    for (int s = 0; s < p.splits; s++) {
+      const float4* src = reinterpret_cast<const float4*>(partial_row(p, s, b, m) + n0);
+#pragma unroll
+      for (int q = 0; q < 8; q++) {
+        const float4 v = __ldcg(src + q);
+        r[4 * q + 0] = __float_as_uint(__fadd_rn(__uint_as_float(r[4 * q + 0]), v.x));
+        r[4 * q + 1] = __float_as_uint(__fadd_rn(__uint_as_float(r[4 * q + 1]), v.y));
+        r[4 * q + 2] = __float_as_uint(__fadd_rn(__uint_as_float(r[4 * q + 2]), v.z));
+        r[4 * q + 3] = __float_as_uint(__fadd_rn(__uint_as_float(r[4 * q + 3]), v.w));
+      }
+    }
+  } else {
+#pragma unroll
+    for (int j = 0; j < 32; j++) {
+      float acc = 0.0f;
+      if (m < p.M && n0 + j < p.N)
+        for (int s = 0; s < p.splits; s++) acc = __fadd_rn(acc, __ldcg(partial_row(p, s, b, m) + n0 + j));
+      r[j] = __float_as_uint(acc);
+    }
+  }
+  store_group(p, r, b, m0, n0, stage, false, 0);
 }
 
 template <int BN, bool TF32X3>
@@ -250,6 +292,7 @@ __global__ void __launch_bounds__(Cfg<BN, TF32X3>::THREADS, 1)
   uint64_t* tempty = tfull + 2;
   uint64_t* drain = tempty + 2;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain + 1);
+  float* epi_stage = reinterpret_cast<float*>(reinterpret_cast<uint8_t*>(bars) + ((C::BAR_BYTES + 15) / 16) * 16);
 
   const int warp = threadIdx.x / 32;
   const int lane = threadIdx.x & 31;
@@ -409,19 +452,21 @@ __global__ void __launch_bounds__(Cfg<BN, TF32X3>::THREADS, 1)
     // ---------------- epilogue ----------------
     const int q = warp & 3;
     const uint32_t lane_base = tmem_base + ((uint32_t)(q * 32) << 16);
+    float* stage = epi_stage + (warp - 2) * (32 * 33);
+    const bool split_mode = p.splits > 1;
     int32_t h = 0;
     bool ok = true;
     for (int32_t u = blockIdx.x; ok && u < p.units; u += gridDim.x) {
       int32_t b, split, tm, tn;
       unit_coords(p, u, &b, &split, &tm, &tn);
-      const int32_t m = tm * kBM + q * 32 + lane;
+      const int32_t m0 = tm * kBM + q * 32;
       const int32_t kb = split * p.kt_per_split;
       const int32_t ke = min(kb + p.kt_per_split, p.k_tiles);
       if constexpr (TF32X3) {
-        // running sum of the chunk accumulators, round-to-nearest f32 adds
-        float run[BN];
-#pragma unroll
-        for (int j = 0; j < BN; j++) run[j] = 0.0f;
+        // Running sum of the chunk accumulators, kept in a third TMEM region (columns 2*BN..3*BN)
+        // and updated with round-to-nearest f32 adds.
+        const uint32_t run_base = lane_base + 2 * BN;
+        bool first = true;
         for (int32_t c0 = kb; c0 < ke; c0 += C::KC, h++) {
           const int acc = h & 1;
           if (!lcd::mbar_wait(&tfull[acc], (h >> 1) & 1, p.err)) {
@@ -429,24 +474,32 @@ __global__ void __launch_bounds__(Cfg<BN, TF32X3>::THREADS, 1)
             break;
           }
           lcd::tc_fence_after();
-#pragma unroll
+#pragma unroll 1
           for (int g = 0; g < BN / 32; g++) {
             uint32_t r[32];
             lcd::tmem_ld_32x32b_x32(lane_base + acc * BN + g * 32, r);
             lcd::tmem_ld_wait();
+            if (!first) {
+              uint32_t q[32];
+              lcd::tmem_ld_32x32b_x32(run_base + g * 32, q);
+              lcd::tmem_ld_wait();
 #pragma unroll
-            for (int j = 0; j < 32; j++) run[g * 32 + j] = __fadd_rn(run[g * 32 + j], __uint_as_float(r[j]));
+              for (int j = 0; j < 32; j++) r[j] = __float_as_uint(__fadd_rn(__uint_as_float(q[j]), __uint_as_float(r[j])));
+            }
+            lcd::tmem_st_32x32b_x32(run_base + g * 32, r);
+            lcd::tmem_st_wait();
           }
+          first = false;
           lcd::tc_fence_before();
           lcd::mbar_arrive(&tempty[acc]);
         }
         if (!ok) break;
-#pragma unroll
+#pragma unroll 1
         for (int g = 0; g < BN / 32; g++) {
           uint32_t r[32];
-#pragma unroll
-          for (int j = 0; j < 32; j++) r[j] = __float_as_uint(run[g * 32 + j]);
-          if (tn * BN + g * 32 < p.N) epilogue_group(p, r, b, split, m, tn * BN + g * 32);
+          lcd::tmem_ld_32x32b_x32(run_base + g * 32, r);
+          lcd::tmem_ld_wait();
+          if (tn * BN + g * 32 < p.N) store_group(p, r, b, m0, tn * BN + g * 32, stage, split_mode, split);
         }
       } else {
         (void)kb;
@@ -459,11 +512,31 @@ __global__ void __launch_bounds__(Cfg<BN, TF32X3>::THREADS, 1)
           uint32_t r[32];
           lcd::tmem_ld_32x32b_x32(lane_base + acc * BN + c0, r);
           lcd::tmem_ld_wait();
-          if (tn * BN + c0 < p.N) epilogue_group(p, r, b, split, m, tn * BN + c0);
+          if (tn * BN + c0 < p.N) store_group(p, r, b, m0, tn * BN + c0, stage, split_mode, split);
         }
         lcd::tc_fence_before();
         lcd::mbar_arrive(&tempty[acc]);
         h++;
+      }
+      if (split_mode && p.fixup) {
+        // Split-K fixup without a second launch.  Each epilogue warp owns 32 rows of the tile:
+        // it publishes its partial rows, counts its arrival on the (tile, warp) counter, and the
+        // warp whose arrival completes the count sums all splits' partial rows in split order
+        // (the same order whoever arrives last, so the result is deterministic) and stores C.
+        // No warp ever waits for another.
+        __threadfence();
+        __syncwarp();
+        const int32_t slot = ((b * p.tiles_m + tm) * p.tiles_n + tn) * 4 + q;
+        uint32_t last = 0;
+        if (lane == 0) last = atomicAdd(&p.counters[slot], 1) == p.splits - 1 ? 1u : 0u;
+        last = __shfl_sync(0xffffffffu, last, 0);
+        if (last) {
+          __threadfence();
+#pragma unroll 1
+          for (int c0 = 0; c0 < BN; c0 += 32)
+            if (tn * BN + c0 < p.N) reduce_group(p, b, m0, tn * BN + c0, stage);
+          if (lane == 0) p.counters[slot] = 0;  // ready for the next launch that reuses the counters
+        }
       }
     }
   } else if constexpr (TF32X3) {
@@ -525,18 +598,35 @@ __global__ void __launch_bounds__(Cfg<BN, TF32X3>::THREADS, 1)
   }
 }
 
-// ---- split-K reduce: C = alpha * sum_s partial[s] + beta * C, splits summed in order -------------
-__global__ void __launch_bounds__(256) splitk_reduce_kernel(const float* __restrict__ partial, KParams p) {
-  const int64_t per = (int64_t)p.M * p.N;
-  const int64_t total = per * p.batch;
+// ---- split-K reduce for many splits: C = epilogue(sum_s partial[s]), splits summed in order -----
+// One thread per 4 consecutive columns of one row (16-byte partial loads); used when so many
+// splits share a tile that reducing inside the GEMM would serialise on a few warps.
+__global__ void __launch_bounds__(256) splitk_reduce_kernel(KParams p) {
+  const int32_t nq = (p.N + 3) / 4;  // column quads per row
+  const int64_t rows = (int64_t)p.batch * p.M;
+  const int64_t total = rows * nq;
+  const int64_t plane = rows * (int64_t)p.N;
   const int64_t stride = (int64_t)gridDim.x * blockDim.x;
+  const bool vec = (p.N % 4) == 0;
   for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < total; i += stride) {
-    float acc = 0.0f;
-    for (int s = 0; s < p.splits; s++) acc = __fadd_rn(acc, partial[(int64_t)s * total + i]);
-    const int64_t b = i / per;
-    const int64_t rem = i - b * per;
-    const int64_t m = rem / p.N, n = rem - (rem / p.N) * p.N;
-    apply_store(p, p.c_off + b * p.c_bs + m * p.c_ms + n * p.c_ns, acc);
+    const int64_t row = i / nq;
+    const int32_t n0 = (int32_t)(i - row * nq) * 4;
+    const int32_t b = (int32_t)(row / p.M), m = (int32_t)(row - (int64_t)b * p.M);
+    float acc[4] = {0.f, 0.f, 0.f, 0.f};
+    const float* src = p.partial + row * p.N + n0;
+    for (int s = 0; s < p.splits; s++, src += plane) {
+      if (vec) {
+        const float4 v = __ldcs(reinterpret_cast<const float4*>(src));
+        acc[0] = __fadd_rn(acc[0], v.x);
+        acc[1] = __fadd_rn(acc[1], v.y);
+        acc[2] = __fadd_rn(acc[2], v.z);
+        acc[3] = __fadd_rn(acc[3], v.w);
+      } else {
+        for (int e = 0; e < 4 && n0 + e < p.N; e++) acc[e] = __fadd_rn(acc[e], src[e]);
+      }
+    }
+    const int64_t base = p.c_off + (int64_t)b * p.c_bs + (int64_t)m * p.c_ms;
+    for (int e = 0; e < 4 && n0 + e < p.N; e++) apply_store(p, base + (int64_t)(n0 + e) * p.c_ns, acc[e]);
   }
 }
 
@@ -575,11 +665,47 @@ EncodeTiledFn encode_fn() {
   return fn;
 }
 
+// Encoded maps are cached by everything that goes into them (a map holds only the address,
+// extents, strides, box and swizzle), so repeated products on the same buffers, such as a
+// pipeline's GEMMs every step, skip the driver call.
+struct MapKey {
+  const void* base;
+  uint64_t inner, rows, batch, rs, bs;
+  uint32_t bi, br;
+  int dt;
+  bool atom32;
+  bool operator==(const MapKey& o) const {
+    return base == o.base && inner == o.inner && rows == o.rows && batch == o.batch && rs == o.rs && bs == o.bs &&
+           bi == o.bi && br == o.br && dt == o.dt && atom32 == o.atom32;
+  }
+};
+struct MapKeyHash {
+  size_t operator()(const MapKey& k) const {
+    uint64_t h = reinterpret_cast<uintptr_t>(k.base);
+    for (uint64_t v : {k.inner, k.rows, k.batch, k.rs, k.bs, (uint64_t)k.bi << 32 | k.br,
+                       (uint64_t)k.dt << 1 | (k.atom32 ? 1u : 0u)})
+      h = (h ^ v) * 0x100000001b3ull;
+    return (size_t)h;
+  }
+};
+std::mutex g_map_mu;
+std::unordered_map<MapKey, CUtensorMap, MapKeyHash> g_maps;
+constexpr size_t kMapCacheMax = 16384;
+
 // 3-D map over (packed axis, row axis, batch) with a 128-byte-swizzled box of box_inner x box_rows.
 // `atom32` selects the 32-byte-atom variant of the 128-byte swizzle (MN-major f32 tiles).
 lc_status make_map(CUtensorMap* map, const void* base, int in_dtype, uint64_t inner, uint64_t rows,
                    uint64_t batch, uint64_t row_stride_b, uint64_t batch_stride_b, uint32_t box_inner,
                    uint32_t box_rows, bool atom32 = false) {
+  const MapKey key{base, inner, rows, batch, row_stride_b, batch_stride_b, box_inner, box_rows, in_dtype, atom32};
+  {
+    std::lock_guard<std::mutex> g(g_map_mu);
+    auto it = g_maps.find(key);
+    if (it != g_maps.end()) {
+      *map = it->second;
+      return LC_OK;
+    }
+  }
   EncodeTiledFn fn = encode_fn();
   if (fn == nullptr) return lc::fail(LC_ERR_LAUNCH, "cuTensorMapEncodeTiled is unavailable");
   CUtensorMapDataType dt = in_dtype == LC_F32    ? CU_TENSOR_MAP_DATA_TYPE_FLOAT32
@@ -593,6 +719,9 @@ lc_status make_map(CUtensorMap* map, const void* base, int in_dtype, uint64_t in
                   atom32 ? CU_TENSOR_MAP_SWIZZLE_128B_ATOM_32B : CU_TENSOR_MAP_SWIZZLE_128B,
                   CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
   if (r != CUDA_SUCCESS) return lc::fail(LC_ERR_LAUNCH, "cuTensorMapEncodeTiled failed (" + std::to_string((int)r) + ")");
+  std::lock_guard<std::mutex> g(g_map_mu);
+  if (g_maps.size() >= kMapCacheMax) g_maps.clear();
+  g_maps.emplace(key, *map);
   return LC_OK;
 }
 
@@ -656,13 +785,37 @@ lc_status gemm_run(lc_context* ctx, cudaStream_t s, const GemmProblem& pr, lc_co
   const int64_t tiles_m = ceil_div(M, 128), tiles_n = ceil_div(N, bn);
   const int64_t k_tiles = ceil_div(pr.k, epr);
   const int64_t tiles = tiles_m * tiles_n * pr.batch;
+  // Split-K choice: the CTAs are persistent, one per SM, so a unit count just above a multiple
+  // of the SM count costs a whole extra wave.  Cost of s splits, in k-tile times along the
+  // critical path: waves(s) * (k-tiles per unit + the unit's partial write and reduce read,
+  // expressed in k-tile loads).  The cheapest s wins; ties go to fewer splits.
+  const int64_t sms = std::max<int64_t>(1, ctx->sm_count - pr.reserve_sms);
+  const double tile_load = (double)(128 + bn) * 128.0;
+  const double partial_cost = (128.0 * bn * 4.0 * 2.0) / tile_load;
+  auto split_cost = [&](int64_t s) {
+    const int64_t per = ceil_div(k_tiles, s);
+    const int64_t real = ceil_div(k_tiles, per);
+    const int64_t waves = ceil_div(tiles * real, sms);
+    return (double)waves * ((double)per + (real > 1 ? partial_cost : 0.0));
+  };
   int64_t splits = 1, kps = k_tiles;
-  if (pr.splits_hint > 0) {
-    splits = std::min<int64_t>(pr.splits_hint, k_tiles);
-  } else if (tiles < ctx->sm_count && k_tiles >= 8) {
-    splits = std::min<int64_t>(ceil_div(ctx->sm_count, tiles), k_tiles / 4);
-    splits = std::max<int64_t>(splits, 1);
+  static const int64_t env_splits = [] {
+    const char* e = getenv("LC_SPLITK");  // tuning override for sweeps; unset in normal use
+    return e ? atoll(e) : 0ll;
+  }();
+  if (pr.splits_hint > 0 || env_splits > 0) {
+    splits = std::min<int64_t>(pr.splits_hint > 0 ? pr.splits_hint : env_splits, k_tiles);
+  } else {
+    double best = split_cost(1);
+    for (int64_t s = 2; s <= std::min<int64_t>(k_tiles, 512); s++) {
+      const double c = split_cost(s);
+      if (c < best * 0.999) {
+        best = c;
+        splits = s;
+      }
+    }
   }
+  splits = std::max<int64_t>(splits, 1);
   kps = ceil_div(k_tiles, splits);
   splits = ceil_div(k_tiles, kps);
   const int64_t units = tiles * splits;
@@ -736,20 +889,52 @@ lc_status gemm_run(lc_context* ctx, cudaStream_t s, const GemmProblem& pr, lc_co
   p.aux = pr.aux;
   p.aux2 = pr.aux2;
   p.lr = pr.lr;
-  auto rows_aligned = [&](const void* base, size_t es) {
-    return c_ns == 1 && ((reinterpret_cast<uintptr_t>(base) + pr.c_offset * es) % 16 == 0) &&
-           ((c_ms * es) % 16 == 0 || M == 1) && ((pr.c_batch_stride * es) % 16 == 0 || pr.batch == 1);
-  };
-  if (pr.epi == 2)
-    p.vec_ok = rows_aligned(pr.aux, 4) && rows_aligned(pr.aux2, 2) ? 1 : 0;
-  else
-    p.vec_ok = rows_aligned(pr.c, dtype_size(pr.c_dtype)) ? 1 : 0;
-  float* partial = nullptr;
+  // Split-K scratch: the partial tiles and, for the in-kernel fixup (up to kFixupMaxSplits splits,
+  // where each reducing warp sums few partials), one arrival counter per (batch, tile, epilogue
+  // warp).  On the context's own stream the context keeps both between calls (its counters are
+  // zero between launches: each fixup resets what it used); on any other stream they come from
+  // the stream-ordered pool, counters zeroed in stream order.
+  constexpr int64_t kFixupMaxSplits = 4;
+  void* scratch = nullptr;
   if (splits > 1) {
-    st = scratch_alloc(ctx, s, sizeof(float) * (size_t)splits * pr.batch * M * N, (void**)&partial);
-    if (st) return st;
-    p.mode = 1;
-    p.partial = partial;
+    p.fixup = splits <= kFixupMaxSplits ? 1 : 0;
+    const size_t part_bytes = sizeof(float) * (size_t)splits * pr.batch * M * N;
+    const size_t part_pad = (part_bytes + 255) / 256 * 256;
+    const size_t cnt_n = (size_t)tiles * 4;
+    if (s == ctx->stream) {
+      if (ctx->split_part_bytes < part_pad || ctx->split_cnt_n < cnt_n) {
+        cudaError_t e = cudaStreamSynchronize(s);
+        if (e == cudaSuccess && ctx->split_part_bytes < part_pad) {
+          if (ctx->split_part) cudaFree(ctx->split_part);
+          ctx->split_part = nullptr;
+          ctx->split_part_bytes = 0;
+          e = cudaMalloc(&ctx->split_part, part_pad);
+          if (e == cudaSuccess) ctx->split_part_bytes = part_pad;
+        }
+        if (e == cudaSuccess && ctx->split_cnt_n < cnt_n) {
+          if (ctx->split_cnt) cudaFree(ctx->split_cnt);
+          ctx->split_cnt = nullptr;
+          ctx->split_cnt_n = 0;
+          const size_t n = std::max<size_t>(cnt_n, 4096);
+          e = cudaMalloc(&ctx->split_cnt, n * sizeof(int));
+          if (e == cudaSuccess) e = cudaMemsetAsync(ctx->split_cnt, 0, n * sizeof(int), s);
+          if (e == cudaSuccess) ctx->split_cnt_n = n;
+        }
+        if (e != cudaSuccess) return cuda_fail(e, "split-K scratch");
+      }
+      p.partial = static_cast<float*>(ctx->split_part);
+      p.counters = ctx->split_cnt;
+    } else {
+      st = scratch_alloc(ctx, s, part_pad + cnt_n * sizeof(int), &scratch);
+      if (st) return st;
+      p.partial = static_cast<float*>(scratch);
+      p.counters = reinterpret_cast<int*>(static_cast<uint8_t*>(scratch) + part_pad);
+      cudaError_t e = p.fixup ? cudaMemsetAsync(p.counters, 0, cnt_n * sizeof(int), s) : cudaSuccess;
+      if (e != cudaSuccess) {
+        scratch_free(scratch, s);
+        return cuda_fail(e, "split-K counters");
+      }
+    }
   }
   const int grid = (int)std::max<int64_t>(1, std::min<int64_t>(units, ctx->sm_count - pr.reserve_sms));
   if (tf32x3) {
@@ -759,17 +944,15 @@ lc_status gemm_run(lc_context* ctx, cudaStream_t s, const GemmProblem& pr, lc_co
          : bn == 128 ? launch_kernel<128, false>(ctx, s, ta, tb, p, grid)
                      : launch_kernel<256, false>(ctx, s, ta, tb, p, grid);
   }
-  if (st == LC_OK && splits > 1) {
-    KParams rp = p;
-    rp.mode = 0;
-    const int64_t total = (int64_t)pr.batch * M * N;
-    const int rgrid = (int)std::min<int64_t>(ceil_div(total, 256), (int64_t)ctx->sm_count * 8);
-    splitk_reduce_kernel<<<rgrid, 256, 0, s>>>(partial, rp);
+  if (st == LC_OK && splits > 1 && !p.fixup) {
+    const int64_t quads = (int64_t)pr.batch * M * ((N + 3) / 4);
+    const int rgrid = (int)std::max<int64_t>(1, std::min<int64_t>(ceil_div(quads, 256), (int64_t)ctx->sm_count * 8));
+    splitk_reduce_kernel<<<rgrid, 256, 0, s>>>(p);
     record_launch(ctx, "gemm_splitk_reduce");
     cudaError_t e = cudaGetLastError();
     if (e != cudaSuccess) st = cuda_fail(e, "split-K reduce launch");
   }
-  if (partial) scratch_free(partial, s);
+  if (scratch) scratch_free(scratch, s);
   return st;
 }
 

@@ -18,6 +18,12 @@ struct lc_context {
   std::atomic<uint64_t> launches{0};
   std::mutex names_mu;
   std::vector<const char*> names;  // ring of the most recent launch names
+  // Split-K scratch reused by every GEMM launched on the context's own stream (stream order makes
+  // reuse safe): partial tiles, and arrival counters that each launch leaves at zero again.
+  void* split_part = nullptr;
+  size_t split_part_bytes = 0;
+  int* split_cnt = nullptr;
+  size_t split_cnt_n = 0;
 };
 
 namespace lc {
