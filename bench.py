@@ -292,7 +292,7 @@ def run_profile(args):
         ctx.sync()
         print(json.dumps({"profile": "gemm", "launches": ctx.debug_launches()[-8:]}))
         return 0
-    p = Pipeline(LAYERS, WIDTH, MB, MBS, lr=LR)
+    p = Pipeline(args.layers, WIDTH, MB, MBS, lr=LR)
     p.init_weights(1234, WIDTH ** -0.5)
     x = torch.from_numpy(data.normal(1, (BATCH, WIDTH))).cuda()
     t = torch.from_numpy(data.normal(2, (BATCH, WIDTH))).cuda()
@@ -313,6 +313,7 @@ def main():
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--no-extras", action="store_true", help="skip the N=1 contraction/op figures")
+    ap.add_argument("--layers", type=int, default=LAYERS, help="profiling driver only: pipeline depth")
     ap.add_argument("--profile", choices=["step", "gemm"], default=None,
                     help="profiling driver: 'step' runs --warmup + --steps pipeline steps and nothing else; "
                          "'gemm' runs --steps forward-shaped GEMMs ([64,8192] x [8192,8192] bf16)")

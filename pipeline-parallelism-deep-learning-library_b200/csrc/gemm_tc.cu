@@ -27,6 +27,7 @@
 #include <cstring>
 #include <mutex>
 #include <string>
+#include <type_traits>
 #include <unordered_map>
 
 #include "gemm.h"
@@ -54,8 +55,8 @@ struct KParams {
   float* partial;   // split-K: [splits][batch][M][N] raw partial sums
   int* counters;    // split-K fixup: one arrival counter per (batch, tile, epilogue warp), zero at launch
   int32_t fixup;    // 1: the last-arriving warp reduces in the kernel; 0: a separate reduce kernel does
+  int32_t vec;      // C's columns contiguous and every row start 16-byte aligned (C, aux and aux2)
   int* err;
-  int32_t epi;       // 0 standard, 1 ReLU-mask by aux, 2 fused SGD into aux (f32) / aux2 (bf16)
   const void* aux;
   void* aux2;
   float lr;
@@ -82,8 +83,7 @@ struct Cfg {
   // about 24 ulp-halves per chunk while the chunks themselves are summed round-to-nearest.
   static constexpr int KC = TF32X3 ? 2 : (1 << 30);
   static constexpr int BAR_BYTES = 8 * (3 * STAGES + 5) + 16;
-  static constexpr int EPI_STAGE_BYTES = 4 * 32 * 33 * 4;  // one 32x33 f32 transpose tile per epilogue warp
-  static constexpr int SMEM = STAGES * STAGE_BYTES + ((BAR_BYTES + 15) / 16) * 16 + EPI_STAGE_BYTES + 1024;
+  static constexpr int SMEM = STAGES * STAGE_BYTES + ((BAR_BYTES + 15) / 16) * 16 + 1024;
   static_assert(STAGES >= 2, "at least two stages");
 };
 
@@ -119,10 +119,17 @@ __device__ __forceinline__ float load_c(const KParams& p, int64_t idx) {
   return __half2float(__ushort_as_half(h));
 }
 
+__device__ __forceinline__ uint16_t to_half_bits(const KParams& p, float v) {
+  return p.c_dtype == LC_BF16 ? f32_to_bf16_rne(v) : __half_as_ushort(__float2half_rn(v));
+}
+
+__device__ __forceinline__ float from_half_bits(const KParams& p, uint16_t h) {
+  return p.c_dtype == LC_BF16 ? __uint_as_float(((uint32_t)h) << 16) : __half2float(__ushort_as_half(h));
+}
+
 __device__ __forceinline__ void store_c(const KParams& p, int64_t idx, float v) {
   if (p.c_dtype == LC_F32) static_cast<float*>(p.c)[idx] = v;
-  else if (p.c_dtype == LC_BF16) static_cast<uint16_t*>(p.c)[idx] = f32_to_bf16_rne(v);
-  else static_cast<uint16_t*>(p.c)[idx] = __half_as_ushort(__float2half_rn(v));
+  else static_cast<uint16_t*>(p.c)[idx] = to_half_bits(p, v);
 }
 
 __device__ __forceinline__ float finish(const KParams& p, float acc, float cold) {
@@ -132,146 +139,192 @@ __device__ __forceinline__ float finish(const KParams& p, float acc, float cold)
   return v;
 }
 
-__device__ __forceinline__ bool mask_on(const KParams& p, int64_t idx) {
-  const uint16_t h = static_cast<const uint16_t*>(p.aux)[idx];
-  return __uint_as_float(((uint32_t)h) << 16) > 0.0f;
+// ---- epilogue variants ---------------------------------------------------------------------------
+// EPI is a template parameter so that each kernel instance carries only its own epilogue:
+//   0  C = alpha * acc + beta * C, optional ReLU; C f32 / bf16 / f16 with any strides;
+//   1  C = alpha * acc where aux > 0, else +0 (aux: bf16 laid out like C) -- the ReLU derivative
+//      fused into the data-gradient product;
+//   2  master = master - lr * (alpha * acc), aux2 = bf16(master) (aux: f32 master, aux2: bf16 copy,
+//      both laid out like C; C itself is unused) -- the SGD step fused into the weight gradient.
+// `old` is what the variant reads before it writes: C (EPI 0, beta != 0), the mask (1), master (2).
+
+template <int EPI>
+__device__ __forceinline__ float read_old(const KParams& p, int64_t idx) {
+  if constexpr (EPI == 0) return p.beta != 0.0f ? load_c(p, idx) : 0.0f;
+  else if constexpr (EPI == 1) return __uint_as_float(((uint32_t) static_cast<const uint16_t*>(p.aux)[idx]) << 16);
+  else return static_cast<const float*>(p.aux)[idx];
 }
 
-// One output element through the selected epilogue (scalar path and split-K reduce).
-__device__ __forceinline__ void apply_store(const KParams& p, int64_t idx, float acc) {
-  if (p.epi == 0) {
-    const float cold = p.beta != 0.0f ? load_c(p, idx) : 0.0f;
-    store_c(p, idx, finish(p, acc, cold));
-  } else if (p.epi == 1) {
-    store_c(p, idx, mask_on(p, idx) ? __fmul_rn(p.alpha, acc) : 0.0f);
+template <int EPI>
+__device__ __forceinline__ void write_new(const KParams& p, int64_t idx, float acc, float old) {
+  if constexpr (EPI == 0) {
+    store_c(p, idx, finish(p, acc, old));
+  } else if constexpr (EPI == 1) {
+    store_c(p, idx, old > 0.0f ? __fmul_rn(p.alpha, acc) : 0.0f);
   } else {
-    float* master = static_cast<float*>(const_cast<void*>(p.aux));
-    const float step = __fmul_rn(p.lr, __fmul_rn(p.alpha, acc));
-    const float w = __fsub_rn(master[idx], step);
-    master[idx] = w;
+    const float w = __fsub_rn(old, __fmul_rn(p.lr, __fmul_rn(p.alpha, acc)));
+    static_cast<float*>(const_cast<void*>(p.aux))[idx] = w;
     static_cast<uint16_t*>(p.aux2)[idx] = f32_to_bf16_rne(w);
   }
+}
+
+// Epilogue of the 32 consecutive kernel columns [n0, n0 + cnt) of one kernel row, held by one
+// thread in v[]; `base` is the C index of (row, n0).  Every read goes out before the first write,
+// so the loads overlap instead of queueing behind stores the compiler cannot prove disjoint.
+//  * p.vec (C's columns contiguous, every row start 16-byte aligned): 16-byte loads and stores,
+//    one thread covering 64 or 128 contiguous bytes per array;
+//  * otherwise element by element at stride c_ns.  In the swapped skinny products C's kernel
+//    rows are its columns (c_ms == 1), so the 32 lanes of a warp, which hold 32 consecutive
+//    kernel rows, touch 32 consecutive elements per store.
+template <int EPI>
+__device__ __forceinline__ void store_row(const KParams& p, const float (&v)[32], int64_t base, int32_t cnt) {
+  if (p.vec && cnt == 32) {
+    if constexpr (EPI == 2) {
+      float* master = static_cast<float*>(const_cast<void*>(p.aux)) + base;
+      uint16_t* wb = static_cast<uint16_t*>(p.aux2) + base;
+      float4 w[8];
+#pragma unroll
+      for (int q = 0; q < 8; q++) w[q] = *reinterpret_cast<const float4*>(master + 4 * q);
+#pragma unroll
+      for (int q = 0; q < 8; q++) {
+        w[q].x = __fsub_rn(w[q].x, __fmul_rn(p.lr, __fmul_rn(p.alpha, v[4 * q + 0])));
+        w[q].y = __fsub_rn(w[q].y, __fmul_rn(p.lr, __fmul_rn(p.alpha, v[4 * q + 1])));
+        w[q].z = __fsub_rn(w[q].z, __fmul_rn(p.lr, __fmul_rn(p.alpha, v[4 * q + 2])));
+        w[q].w = __fsub_rn(w[q].w, __fmul_rn(p.lr, __fmul_rn(p.alpha, v[4 * q + 3])));
+        *reinterpret_cast<float4*>(master + 4 * q) = w[q];
+      }
+#pragma unroll
+      for (int q = 0; q < 4; q++) {
+        uint4 out;
+        out.x = f32_to_bf16_rne(w[2 * q].x) | ((uint32_t)f32_to_bf16_rne(w[2 * q].y) << 16);
+        out.y = f32_to_bf16_rne(w[2 * q].z) | ((uint32_t)f32_to_bf16_rne(w[2 * q].w) << 16);
+        out.z = f32_to_bf16_rne(w[2 * q + 1].x) | ((uint32_t)f32_to_bf16_rne(w[2 * q + 1].y) << 16);
+        out.w = f32_to_bf16_rne(w[2 * q + 1].z) | ((uint32_t)f32_to_bf16_rne(w[2 * q + 1].w) << 16);
+        *reinterpret_cast<uint4*>(wb + 8 * q) = out;
+      }
+      return;
+    } else {
+      // values read first (C for beta, or the bf16 mask), as 32 floats
+      float old[32];
+      const bool reads = EPI == 1 || p.beta != 0.0f;
+      if (reads) {
+        if (EPI == 0 && p.c_dtype == LC_F32) {
+          const float4* src = reinterpret_cast<const float4*>(static_cast<const float*>(p.c) + base);
+#pragma unroll
+          for (int q = 0; q < 8; q++) {
+            const float4 o = src[q];
+            old[4 * q] = o.x;
+            old[4 * q + 1] = o.y;
+            old[4 * q + 2] = o.z;
+            old[4 * q + 3] = o.w;
+          }
+        } else {
+          const uint4* src = reinterpret_cast<const uint4*>(
+              static_cast<const uint16_t*>(EPI == 1 ? p.aux : static_cast<const void*>(p.c)) + base);
+          uint4 raw[4];
+#pragma unroll
+          for (int q = 0; q < 4; q++) raw[q] = src[q];
+#pragma unroll
+          for (int q = 0; q < 4; q++) {
+            const uint32_t w4[4] = {raw[q].x, raw[q].y, raw[q].z, raw[q].w};
+#pragma unroll
+            for (int e = 0; e < 4; e++) {
+              const uint16_t lo = (uint16_t)(w4[e] & 0xffffu), hi = (uint16_t)(w4[e] >> 16);
+              if (EPI == 1) {
+                old[8 * q + 2 * e] = __uint_as_float((uint32_t)lo << 16);
+                old[8 * q + 2 * e + 1] = __uint_as_float((uint32_t)hi << 16);
+              } else {
+                old[8 * q + 2 * e] = from_half_bits(p, lo);
+                old[8 * q + 2 * e + 1] = from_half_bits(p, hi);
+              }
+            }
+          }
+        }
+      }
+      float out[32];
+#pragma unroll
+      for (int j = 0; j < 32; j++) {
+        if constexpr (EPI == 0) out[j] = finish(p, v[j], reads ? old[j] : 0.0f);
+        else out[j] = old[j] > 0.0f ? __fmul_rn(p.alpha, v[j]) : 0.0f;
+      }
+      if (p.c_dtype == LC_F32) {
+        float4* dst = reinterpret_cast<float4*>(static_cast<float*>(p.c) + base);
+#pragma unroll
+        for (int q = 0; q < 8; q++) dst[q] = make_float4(out[4 * q], out[4 * q + 1], out[4 * q + 2], out[4 * q + 3]);
+      } else {
+        uint4* dst = reinterpret_cast<uint4*>(static_cast<uint16_t*>(p.c) + base);
+#pragma unroll
+        for (int q = 0; q < 4; q++) {
+          uint4 o;
+          o.x = to_half_bits(p, out[8 * q + 0]) | ((uint32_t)to_half_bits(p, out[8 * q + 1]) << 16);
+          o.y = to_half_bits(p, out[8 * q + 2]) | ((uint32_t)to_half_bits(p, out[8 * q + 3]) << 16);
+          o.z = to_half_bits(p, out[8 * q + 4]) | ((uint32_t)to_half_bits(p, out[8 * q + 5]) << 16);
+          o.w = to_half_bits(p, out[8 * q + 6]) | ((uint32_t)to_half_bits(p, out[8 * q + 7]) << 16);
+          dst[q] = o;
+        }
+      }
+      return;
+    }
+  }
+  float old[32];
+  const bool reads = EPI != 0 || p.beta != 0.0f;
+  if (reads) {
+#pragma unroll
+    for (int j = 0; j < 32; j++) old[j] = j < cnt ? read_old<EPI>(p, base + (int64_t)j * p.c_ns) : 0.0f;
+  }
+#pragma unroll
+  for (int j = 0; j < 32; j++)
+    if (j < cnt) write_new<EPI>(p, base + (int64_t)j * p.c_ns, v[j], reads ? old[j] : 0.0f);
 }
 
 __device__ __forceinline__ float* partial_row(const KParams& p, int32_t split, int32_t b, int32_t m) {
   return p.partial + (((int64_t)split * p.batch + b) * p.M + m) * (int64_t)p.N;
 }
 
-// The epilogue of 32 elements at C indices i0 + j*st (bit j of `valid` set when element j exists).
-// Every value the epilogue reads (old C for beta, the ReLU mask, the SGD master weight) is loaded
-// for all 32 elements before the first store, so the loads are in flight together instead of each
-// waiting behind the previous element's store.
-__device__ __forceinline__ void apply32(const KParams& p, const float (&acc)[32], int64_t i0, int64_t st,
-                                        uint32_t valid) {
-  float old[32];
-  // pass 1: every read this epilogue needs, back to back
-  const bool reads = p.epi != 0 || p.beta != 0.0f;
-  if (reads) {
-    int64_t idx = i0;
+// Raw split-K partial of 32 columns of one row: 128 contiguous bytes per thread when they fit.
+__device__ __forceinline__ void store_partial(const KParams& p, const float (&v)[32], float* dst, int32_t cnt) {
+  if (cnt == 32 && (p.N % 4) == 0) {
 #pragma unroll
-    for (int j = 0; j < 32; j++, idx += st) {
-      float o = 0.0f;
-      if ((valid >> j) & 1u) {
-        if (p.epi == 0) o = load_c(p, idx);
-        else if (p.epi == 1) o = __uint_as_float(((uint32_t) static_cast<const uint16_t*>(p.aux)[idx]) << 16);
-        else o = static_cast<const float*>(p.aux)[idx];
-      }
-      old[j] = o;
-    }
-  }
-  // pass 2: compute and store
-  int64_t idx = i0;
+    for (int q = 0; q < 8; q++)
+      reinterpret_cast<float4*>(dst)[q] = make_float4(v[4 * q], v[4 * q + 1], v[4 * q + 2], v[4 * q + 3]);
+  } else {
 #pragma unroll
-  for (int j = 0; j < 32; j++, idx += st) {
-    if (!((valid >> j) & 1u)) continue;
-    if (p.epi == 0) {
-      store_c(p, idx, finish(p, acc[j], reads ? old[j] : 0.0f));
-    } else if (p.epi == 1) {
-      store_c(p, idx, old[j] > 0.0f ? __fmul_rn(p.alpha, acc[j]) : 0.0f);
-    } else {
-      const float w = __fsub_rn(old[j], __fmul_rn(p.lr, __fmul_rn(p.alpha, acc[j])));
-      static_cast<float*>(const_cast<void*>(p.aux))[idx] = w;
-      static_cast<uint16_t*>(p.aux2)[idx] = f32_to_bf16_rne(w);
-    }
+    for (int j = 0; j < 32; j++)
+      if (j < cnt) dst[j] = v[j];
   }
 }
 
-// Output of one 32-column group [n0, n0 + 32) of the warp's 32 rows [m0, m0 + 32): lane l holds
-// row m0 + l in r[0..31].  When C's columns are contiguous (c_ns == 1), the group goes through the
-// warp's 32x33 shared tile so that every store instruction covers 32 consecutive columns of one
-// row (coalesced); otherwise (the swapped skinny products, whose rows are contiguous) each lane
-// stores its own row and consecutive lanes hit consecutive addresses.  `to_partial` writes the
-// raw accumulator into this split's partial row instead.
-__device__ __forceinline__ void store_group(const KParams& p, const uint32_t (&r)[32], int32_t b, int32_t m0, int32_t n0,
-                                            float* stage, bool to_partial, int32_t split) {
-  const int lane = threadIdx.x & 31;
-  if (to_partial || p.c_ns == 1) {
+// Sum of the splits' partials of 32 columns of one row, in split order from +0 (the order the
+// separate reduce kernel uses too, so the result does not depend on which path reduced).
+__device__ __forceinline__ void sum_partials(const KParams& p, float (&v)[32], int32_t b, int32_t m, int32_t n0,
+                                             int32_t cnt) {
 #pragma unroll
-    for (int j = 0; j < 32; j++) stage[lane * 33 + j] = __uint_as_float(r[j]);
-    __syncwarp();
-    const int32_t n = n0 + lane;
-    float v[32];
-    uint32_t valid = 0;
-#pragma unroll
-    for (int i = 0; i < 32; i++) {
-      v[i] = stage[i * 33 + lane];
-      if (m0 + i < p.M && n < p.N) valid |= 1u << i;
-    }
-    __syncwarp();
-    if (to_partial) {
-      float* dst = partial_row(p, split, b, m0) + n;
-#pragma unroll
-      for (int i = 0; i < 32; i++)
-        if ((valid >> i) & 1u) dst[(int64_t)i * p.N] = v[i];
-    } else {
-      apply32(p, v, p.c_off + (int64_t)b * p.c_bs + (int64_t)m0 * p.c_ms + n, p.c_ms, valid);
-    }
-    return;
-  }
-  const int32_t m = m0 + lane;
-  if (m >= p.M) return;
-  float v[32];
-  uint32_t valid = 0;
-#pragma unroll
-  for (int j = 0; j < 32; j++) {
-    v[j] = __uint_as_float(r[j]);
-    if (n0 + j < p.N) valid |= 1u << j;
-  }
-  apply32(p, v, p.c_off + (int64_t)b * p.c_bs + (int64_t)m * p.c_ms + (int64_t)n0 * p.c_ns, p.c_ns, valid);
-}
-
-// Last CTA of a split tile: sum the splits' partial rows in split order and store the group.
-__device__ __forceinline__ void reduce_group(const KParams& p, int32_t b, int32_t m0, int32_t n0, float* stage) {
-  const int lane = threadIdx.x & 31;
-  uint32_t r[32];
-  const int32_t m = m0 + lane;
-  if (m < p.M && n0 + 32 <= p.N && (p.N % 4) == 0) {
-#pragma unroll
-    for (int j = 0; j < 32; j++) r[j] = 0u;
+  for (int j = 0; j < 32; j++) v[j] = 0.0f;
+  if (cnt == 32 && (p.N % 4) == 0) {
     for (int s = 0; s < p.splits; s++) {
       const float4* src = reinterpret_cast<const float4*>(partial_row(p, s, b, m) + n0);
+      float4 t[8];
+#pragma unroll
+      for (int q = 0; q < 8; q++) t[q] = __ldcg(src + q);
 #pragma unroll
       for (int q = 0; q < 8; q++) {
-        const float4 v = __ldcg(src + q);
-        r[4 * q + 0] = __float_as_uint(__fadd_rn(__uint_as_float(r[4 * q + 0]), v.x));
-        r[4 * q + 1] = __float_as_uint(__fadd_rn(__uint_as_float(r[4 * q + 1]), v.y));
-        r[4 * q + 2] = __float_as_uint(__fadd_rn(__uint_as_float(r[4 * q + 2]), v.z));
-        r[4 * q + 3] = __float_as_uint(__fadd_rn(__uint_as_float(r[4 * q + 3]), v.w));
+        v[4 * q + 0] = __fadd_rn(v[4 * q + 0], t[q].x);
+        v[4 * q + 1] = __fadd_rn(v[4 * q + 1], t[q].y);
+        v[4 * q + 2] = __fadd_rn(v[4 * q + 2], t[q].z);
+        v[4 * q + 3] = __fadd_rn(v[4 * q + 3], t[q].w);
       }
     }
   } else {
+    for (int s = 0; s < p.splits; s++) {
+      const float* src = partial_row(p, s, b, m) + n0;
 #pragma unroll
-    for (int j = 0; j < 32; j++) {
-      float acc = 0.0f;
-      if (m < p.M && n0 + j < p.N)
-        for (int s = 0; s < p.splits; s++) acc = __fadd_rn(acc, __ldcg(partial_row(p, s, b, m) + n0 + j));
-      r[j] = __float_as_uint(acc);
+      for (int j = 0; j < 32; j++)
+        if (j < cnt) v[j] = __fadd_rn(v[j], __ldcg(src + j));
     }
   }
-  store_group(p, r, b, m0, n0, stage, false, 0);
 }
 
-template <int BN, bool TF32X3>
+template <int BN, bool TF32X3, int EPI>
 __global__ void __launch_bounds__(Cfg<BN, TF32X3>::THREADS, 1)
     gemm_tc_kernel(const __grid_constant__ CUtensorMap tma_a, const __grid_constant__ CUtensorMap tma_b,
                    const KParams p) {
@@ -292,7 +345,6 @@ __global__ void __launch_bounds__(Cfg<BN, TF32X3>::THREADS, 1)
   uint64_t* tempty = tfull + 2;
   uint64_t* drain = tempty + 2;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain + 1);
-  float* epi_stage = reinterpret_cast<float*>(reinterpret_cast<uint8_t*>(bars) + ((C::BAR_BYTES + 15) / 16) * 16);
 
   const int warp = threadIdx.x / 32;
   const int lane = threadIdx.x & 31;
@@ -450,21 +502,32 @@ __global__ void __launch_bounds__(Cfg<BN, TF32X3>::THREADS, 1)
     }
   } else if (warp < 6) {
     // ---------------- epilogue ----------------
+    // Warp q owns TMEM lanes (tile rows) 32q..32q+31; lane l holds tile row 32q + l.
     const int q = warp & 3;
     const uint32_t lane_base = tmem_base + ((uint32_t)(q * 32) << 16);
-    float* stage = epi_stage + (warp - 2) * (32 * 33);
     const bool split_mode = p.splits > 1;
     int32_t h = 0;
     bool ok = true;
     for (int32_t u = blockIdx.x; ok && u < p.units; u += gridDim.x) {
       int32_t b, split, tm, tn;
       unit_coords(p, u, &b, &split, &tm, &tn);
-      const int32_t m0 = tm * kBM + q * 32;
-      const int32_t kb = split * p.kt_per_split;
-      const int32_t ke = min(kb + p.kt_per_split, p.k_tiles);
+      const int32_t m = tm * kBM + q * 32 + lane;
+      const int64_t c_row = p.c_off + (int64_t)b * p.c_bs + (int64_t)m * p.c_ms;
+      // one 32-column group [n0, n0 + 32) of this lane's row, straight from the tcgen05.ld registers
+      auto emit = [&](const uint32_t (&r)[32], int32_t n0) {
+        const int32_t cnt = min(32, p.N - n0);
+        if (m >= p.M || cnt <= 0) return;
+        float v[32];
+#pragma unroll
+        for (int j = 0; j < 32; j++) v[j] = __uint_as_float(r[j]);
+        if (split_mode) store_partial(p, v, partial_row(p, split, b, m) + n0, cnt);
+        else store_row<EPI>(p, v, c_row + (int64_t)n0 * p.c_ns, cnt);
+      };
       if constexpr (TF32X3) {
         // Running sum of the chunk accumulators, kept in a third TMEM region (columns 2*BN..3*BN)
         // and updated with round-to-nearest f32 adds.
+        const int32_t kb = split * p.kt_per_split;
+        const int32_t ke = min(kb + p.kt_per_split, p.k_tiles);
         const uint32_t run_base = lane_base + 2 * BN;
         bool first = true;
         for (int32_t c0 = kb; c0 < ke; c0 += C::KC, h++) {
@@ -480,11 +543,11 @@ __global__ void __launch_bounds__(Cfg<BN, TF32X3>::THREADS, 1)
             lcd::tmem_ld_32x32b_x32(lane_base + acc * BN + g * 32, r);
             lcd::tmem_ld_wait();
             if (!first) {
-              uint32_t q[32];
-              lcd::tmem_ld_32x32b_x32(run_base + g * 32, q);
+              uint32_t o[32];
+              lcd::tmem_ld_32x32b_x32(run_base + g * 32, o);
               lcd::tmem_ld_wait();
 #pragma unroll
-              for (int j = 0; j < 32; j++) r[j] = __float_as_uint(__fadd_rn(__uint_as_float(q[j]), __uint_as_float(r[j])));
+              for (int j = 0; j < 32; j++) r[j] = __float_as_uint(__fadd_rn(__uint_as_float(o[j]), __uint_as_float(r[j])));
             }
             lcd::tmem_st_32x32b_x32(run_base + g * 32, r);
             lcd::tmem_st_wait();
@@ -499,20 +562,18 @@ __global__ void __launch_bounds__(Cfg<BN, TF32X3>::THREADS, 1)
           uint32_t r[32];
           lcd::tmem_ld_32x32b_x32(run_base + g * 32, r);
           lcd::tmem_ld_wait();
-          if (tn * BN + g * 32 < p.N) store_group(p, r, b, m0, tn * BN + g * 32, stage, split_mode, split);
+          emit(r, tn * BN + g * 32);
         }
       } else {
-        (void)kb;
-        (void)ke;
         const int acc = h & 1;
         if (!lcd::mbar_wait(&tfull[acc], (h >> 1) & 1, p.err)) break;
         lcd::tc_fence_after();
 #pragma unroll 1
-        for (int c0 = 0; c0 < BN; c0 += 32) {
+        for (int g = 0; g < BN / 32; g++) {
           uint32_t r[32];
-          lcd::tmem_ld_32x32b_x32(lane_base + acc * BN + c0, r);
+          lcd::tmem_ld_32x32b_x32(lane_base + acc * BN + g * 32, r);
           lcd::tmem_ld_wait();
-          if (tn * BN + c0 < p.N) store_group(p, r, b, m0, tn * BN + c0, stage, split_mode, split);
+          emit(r, tn * BN + g * 32);
         }
         lcd::tc_fence_before();
         lcd::mbar_arrive(&tempty[acc]);
@@ -532,9 +593,17 @@ __global__ void __launch_bounds__(Cfg<BN, TF32X3>::THREADS, 1)
         last = __shfl_sync(0xffffffffu, last, 0);
         if (last) {
           __threadfence();
+          if (m < p.M) {
 #pragma unroll 1
-          for (int c0 = 0; c0 < BN; c0 += 32)
-            if (tn * BN + c0 < p.N) reduce_group(p, b, m0, tn * BN + c0, stage);
+            for (int g = 0; g < BN / 32; g++) {
+              const int32_t n0 = tn * BN + g * 32;
+              const int32_t cnt = min(32, p.N - n0);
+              if (cnt <= 0) break;
+              float v[32];
+              sum_partials(p, v, b, m, n0, cnt);
+              store_row<EPI>(p, v, c_row + (int64_t)n0 * p.c_ns, cnt);
+            }
+          }
           if (lane == 0) p.counters[slot] = 0;  // ready for the next launch that reuses the counters
         }
       }
@@ -600,17 +669,32 @@ __global__ void __launch_bounds__(Cfg<BN, TF32X3>::THREADS, 1)
 
 // ---- split-K reduce for many splits: C = epilogue(sum_s partial[s]), splits summed in order -----
 // One thread per 4 consecutive columns of one row (16-byte partial loads); used when so many
-// splits share a tile that reducing inside the GEMM would serialise on a few warps.
-__global__ void __launch_bounds__(256) splitk_reduce_kernel(KParams p) {
+// splits share a tile that reducing inside the GEMM would serialise on a few warps.  Consecutive
+// threads take consecutive rows when C's kernel rows are its contiguous axis (the swapped skinny
+// products), consecutive column quads otherwise, so that C's stores coalesce either way.
+template <int EPI>
+__global__ void __launch_bounds__(256) splitk_reduce_kernel(const KParams p) {
   const int32_t nq = (p.N + 3) / 4;  // column quads per row
   const int64_t rows = (int64_t)p.batch * p.M;
   const int64_t total = rows * nq;
   const int64_t plane = rows * (int64_t)p.N;
   const int64_t stride = (int64_t)gridDim.x * blockDim.x;
   const bool vec = (p.N % 4) == 0;
+  const bool rows_fast = p.c_ms == 1 && p.c_ns != 1;
   for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < total; i += stride) {
-    const int64_t row = i / nq;
-    const int32_t n0 = (int32_t)(i - row * nq) * 4;
+    int64_t row;
+    int32_t quad;
+    if (rows_fast) {
+      const int64_t bq = i / p.M;  // (batch, quad) pair
+      const int32_t m = (int32_t)(i - bq * p.M);
+      const int64_t b = bq / nq;
+      quad = (int32_t)(bq - b * nq);
+      row = b * p.M + m;
+    } else {
+      row = i / nq;
+      quad = (int32_t)(i - row * nq);
+    }
+    const int32_t n0 = quad * 4;
     const int32_t b = (int32_t)(row / p.M), m = (int32_t)(row - (int64_t)b * p.M);
     float acc[4] = {0.f, 0.f, 0.f, 0.f};
     const float* src = p.partial + row * p.N + n0;
@@ -626,7 +710,13 @@ __global__ void __launch_bounds__(256) splitk_reduce_kernel(KParams p) {
       }
     }
     const int64_t base = p.c_off + (int64_t)b * p.c_bs + (int64_t)m * p.c_ms;
-    for (int e = 0; e < 4 && n0 + e < p.N; e++) apply_store(p, base + (int64_t)(n0 + e) * p.c_ns, acc[e]);
+    float old[4];
+#pragma unroll
+    for (int e = 0; e < 4; e++)
+      old[e] = n0 + e < p.N ? read_old<EPI>(p, base + (int64_t)(n0 + e) * p.c_ns) : 0.0f;
+#pragma unroll
+    for (int e = 0; e < 4; e++)
+      if (n0 + e < p.N) write_new<EPI>(p, base + (int64_t)(n0 + e) * p.c_ns, acc[e], old[e]);
   }
 }
 
@@ -725,12 +815,12 @@ lc_status make_map(CUtensorMap* map, const void* base, int in_dtype, uint64_t in
   return LC_OK;
 }
 
-template <int BN, bool TF32X3>
+template <int BN, bool TF32X3, int EPI>
 lc_status launch_kernel(lc_context* ctx, cudaStream_t s, const CUtensorMap& ta, const CUtensorMap& tb, const KParams& p,
                         int grid) {
   using C = Cfg<BN, TF32X3>;
   static bool attr_set[64] = {false};
-  auto kern = gemm_tc_kernel<BN, TF32X3>;
+  auto kern = gemm_tc_kernel<BN, TF32X3, EPI>;
   if (!attr_set[ctx->device % 64]) {
     cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM);
     if (e != cudaSuccess) return lc::cuda_fail(e, "cudaFuncSetAttribute(gemm)");
@@ -885,7 +975,16 @@ lc_status gemm_run(lc_context* ctx, cudaStream_t s, const GemmProblem& pr, lc_co
   p.alpha = pr.alpha;
   p.beta = pr.beta;
   p.err = ctx->d_error;
-  p.epi = pr.epi;
+  if (tf32x3 && pr.epi != 0) return fail(LC_ERR_INVALID_ARGUMENT, "fused epilogues take 16-bit inputs");
+  if (pr.epi < 0 || pr.epi > 2) return fail(LC_ERR_INVALID_ARGUMENT, "unknown epilogue");
+  {
+    // 16-byte vector epilogue: C's columns contiguous, every row start a multiple of 8 elements
+    // from 16-byte-aligned bases (8 covers both 2- and 4-byte elements)
+    auto al16 = [](const void* q) { return (reinterpret_cast<uintptr_t>(q) & 15u) == 0; };
+    const bool strides8 = (p.c_off % 8) == 0 && (p.c_ms % 8) == 0 && (pr.batch == 1 || (p.c_bs % 8) == 0);
+    const bool ptrs = pr.epi == 0 ? al16(pr.c) : pr.epi == 1 ? al16(pr.c) && al16(pr.aux) : al16(pr.aux) && al16(pr.aux2);
+    p.vec = (c_ns == 1 && strides8 && ptrs) ? 1 : 0;
+  }
   p.aux = pr.aux;
   p.aux2 = pr.aux2;
   p.lr = pr.lr;
@@ -938,16 +1037,25 @@ lc_status gemm_run(lc_context* ctx, cudaStream_t s, const GemmProblem& pr, lc_co
   }
   const int grid = (int)std::max<int64_t>(1, std::min<int64_t>(units, ctx->sm_count - pr.reserve_sms));
   if (tf32x3) {
-    st = bn == 64 ? launch_kernel<64, true>(ctx, s, ta, tb, p, grid) : launch_kernel<128, true>(ctx, s, ta, tb, p, grid);
+    st = bn == 64 ? launch_kernel<64, true, 0>(ctx, s, ta, tb, p, grid)
+                  : launch_kernel<128, true, 0>(ctx, s, ta, tb, p, grid);
   } else {
-    st = bn == 64    ? launch_kernel<64, false>(ctx, s, ta, tb, p, grid)
-         : bn == 128 ? launch_kernel<128, false>(ctx, s, ta, tb, p, grid)
-                     : launch_kernel<256, false>(ctx, s, ta, tb, p, grid);
+    auto by_bn = [&](auto epi_tag) {
+      constexpr int E = decltype(epi_tag)::value;
+      return bn == 64    ? launch_kernel<64, false, E>(ctx, s, ta, tb, p, grid)
+             : bn == 128 ? launch_kernel<128, false, E>(ctx, s, ta, tb, p, grid)
+                         : launch_kernel<256, false, E>(ctx, s, ta, tb, p, grid);
+    };
+    st = pr.epi == 0   ? by_bn(std::integral_constant<int, 0>{})
+         : pr.epi == 1 ? by_bn(std::integral_constant<int, 1>{})
+                       : by_bn(std::integral_constant<int, 2>{});
   }
   if (st == LC_OK && splits > 1 && !p.fixup) {
     const int64_t quads = (int64_t)pr.batch * M * ((N + 3) / 4);
     const int rgrid = (int)std::max<int64_t>(1, std::min<int64_t>(ceil_div(quads, 256), (int64_t)ctx->sm_count * 8));
-    splitk_reduce_kernel<<<rgrid, 256, 0, s>>>(p);
+    if (pr.epi == 0) splitk_reduce_kernel<0><<<rgrid, 256, 0, s>>>(p);
+    else if (pr.epi == 1) splitk_reduce_kernel<1><<<rgrid, 256, 0, s>>>(p);
+    else splitk_reduce_kernel<2><<<rgrid, 256, 0, s>>>(p);
     record_launch(ctx, "gemm_splitk_reduce");
     cudaError_t e = cudaGetLastError();
     if (e != cudaSuccess) st = cuda_fail(e, "split-K reduce launch");
