@@ -127,6 +127,20 @@ lc_status lc_encode_gemm(lc_context* ctx, void* stream, float alpha, const lc_vi
                          float beta, const lc_view* c);
 lc_status lc_gemm(lc_context* ctx, float alpha, const lc_view* a, const lc_view* b, float beta,
                   const lc_view* c);
+/* lc_encode_gemm that allocates no device memory (no counterpart in the reference, whose
+ * backends allocate per call).  For callers that must not allocate while they run: a process
+ * that reserves the card's memory up front, where a pool grown mid-step can run out, or a
+ * latency-bound loop that a cudaMalloc/cudaFree or a pool growth would stall.  Same planning,
+ * kernels and results as lc_encode_gemm, with the split-K scratch taken from fixed per-device
+ * arrays: at most 16 MiB of partial sums (splits x batch x M x N f32) and 8192 tile counters,
+ * which it zeroes on the stream before each split launch.  A product whose split does not fit,
+ * or whose operands would need staging copies (no unit stride, or starts/strides not 16-byte
+ * aligned), fails with LC_ERR_INVALID_ARGUMENT and launches nothing.  The arrays are shared by
+ * every context, stream and thread of the process: calls whose kernels may overlap race and
+ * give wrong results, so serialise them.  The first call on a device does set-up (it looks up
+ * the arrays' device addresses); make it before any stream capture. */
+lc_status lc_encode_gemm_noalloc(lc_context* ctx, void* stream, float alpha, const lc_view* a,
+                                 const lc_view* b, float beta, const lc_view* c);
 
 /* Plan summary, for tests and reports (src/ops/contraction.rs:664-675 `Plan`). */
 typedef struct lc_contract_plan {

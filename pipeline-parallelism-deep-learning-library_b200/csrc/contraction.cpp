@@ -566,6 +566,30 @@ lc_status gemm_impl(lc_context* ctx, void* stream, float alpha, const lc_view* a
 
 }  // namespace
 
+namespace lc {
+
+lc_status gemm_fixed_scratch(lc_context* ctx, void* stream, float alpha, const lc_view* a, const lc_view* b, float beta,
+                             const lc_view* c, float* part, size_t part_bytes, int* cnt, size_t cnt_n) {
+  if (ctx == nullptr) return fail(LC_ERR_INVALID_ARGUMENT, "null context");
+  lc_status st = prepare(a, b, c);
+  if (st) return st;
+  Groups g;
+  if ((st = groups_from_gemm(*a, *b, *c, &g))) return st;
+  Plan plan;
+  if ((st = plan_groups(ctx, *a, *b, *c, g, alpha, beta, &plan))) return st;
+  if (plan.stage_a || plan.stage_b || plan.stage_c)
+    return fail(LC_ERR_INVALID_ARGUMENT,
+                "this product needs staging copies of its operands, which the allocation-free entry point "
+                "cannot hold: pass operands with a unit stride and 16-byte aligned starts and strides");
+  plan.prob.fixed_part = part;
+  plan.prob.fixed_part_bytes = part_bytes;
+  plan.prob.fixed_cnt = cnt;
+  plan.prob.fixed_cnt_n = cnt_n;
+  return execute(ctx, stream_of(ctx, stream), plan, nullptr, false);
+}
+
+}  // namespace lc
+
 extern "C" {
 
 lc_status lc_encode_contract(lc_context* ctx, void* stream, float alpha, const lc_view* a, const char* a_labels,

@@ -38,6 +38,13 @@ struct GemmProblem {
   const void* aux = nullptr;
   void* aux2 = nullptr;
   float lr = 0.0f;
+  // Caller-owned split-K scratch (lc_encode_gemm_noalloc): when fixed_part is set, gemm_run takes
+  // the partial sums and arrival counters from here, allocates nothing, zeroes the counters it
+  // will use, and refuses a split that does not fit.  Null: the context's scratch or the pool.
+  float* fixed_part = nullptr;
+  size_t fixed_part_bytes = 0;
+  int* fixed_cnt = nullptr;
+  size_t fixed_cnt_n = 0;
 };
 
 // 0 = K-major, 1 = MN-major, -1 = neither (stage it first).  K-major wins when both apply.
@@ -55,6 +62,11 @@ bool tma_operand_ok(const GemmOperand& o, int in_dtype);
 // Launches the tensor-core GEMM (plus the split-K reduce when it splits).  Operands must pass
 // tma_operand_ok.  With dry_run only `plan` is filled.
 lc_status gemm_run(lc_context* ctx, cudaStream_t s, const GemmProblem& p, lc_contract_plan* plan, bool dry_run);
+
+// lc_encode_gemm's planning and launch with split-K scratch supplied by the caller: refuses
+// products whose operands would need staging copies, or whose split does not fit the scratch.
+lc_status gemm_fixed_scratch(lc_context* ctx, void* stream, float alpha, const lc_view* a, const lc_view* b, float beta,
+                             const lc_view* c, float* part, size_t part_bytes, int* cnt, size_t cnt_n);
 
 // C = beta * C, or zeros when beta == 0 (alpha == 0 or K == 0).
 lc_status gemm_fill(lc_context* ctx, cudaStream_t s, const GemmProblem& p);

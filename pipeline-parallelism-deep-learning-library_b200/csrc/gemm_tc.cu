@@ -1000,7 +1000,23 @@ lc_status gemm_run(lc_context* ctx, cudaStream_t s, const GemmProblem& pr, lc_co
     const size_t part_bytes = sizeof(float) * (size_t)splits * pr.batch * M * N;
     const size_t part_pad = (part_bytes + 255) / 256 * 256;
     const size_t cnt_n = (size_t)tiles * 4;
-    if (s == ctx->stream) {
+    if (pr.fixed_part != nullptr) {
+      if (part_bytes > pr.fixed_part_bytes)
+        return fail(LC_ERR_INVALID_ARGUMENT, "split-K partials need " + std::to_string(part_bytes) +
+                                                 " bytes; the fixed scratch holds " +
+                                                 std::to_string(pr.fixed_part_bytes));
+      if (p.fixup && cnt_n > pr.fixed_cnt_n)
+        return fail(LC_ERR_INVALID_ARGUMENT, "split-K fixup needs " + std::to_string(cnt_n) +
+                                                 " tile counters; the fixed scratch holds " +
+                                                 std::to_string(pr.fixed_cnt_n));
+      p.partial = pr.fixed_part;
+      p.counters = pr.fixed_cnt;
+      // the fixup's arrival counters must start at zero
+      if (p.fixup) {
+        cudaError_t e = cudaMemsetAsync(p.counters, 0, cnt_n * sizeof(int), s);
+        if (e != cudaSuccess) return cuda_fail(e, "split-K counters");
+      }
+    } else if (s == ctx->stream) {
       if (ctx->split_part_bytes < part_pad || ctx->split_cnt_n < cnt_n) {
         cudaError_t e = cudaStreamSynchronize(s);
         if (e == cudaSuccess && ctx->split_part_bytes < part_pad) {

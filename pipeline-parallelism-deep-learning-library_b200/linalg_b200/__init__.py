@@ -103,6 +103,7 @@ def _sig(L):
                                  C.POINTER(lc_contract_plan)]),
         "lc_encode_gemm": (s, [_vp, _vp, f, _V, _V, f, _V]),
         "lc_gemm": (s, [_vp, f, _V, _V, f, _V]),
+        "lc_encode_gemm_noalloc": (s, [_vp, _vp, f, _V, _V, f, _V]),
         "lc_encode_materialize": (s, [_vp, _vp, _V, _V]),
         "lc_materialize": (s, [_vp, _V, _V]),
         "lc_encode_conjugate": (s, [_vp, _vp, _V, _V]),
@@ -344,6 +345,13 @@ def plan_contract(ctx: Context, alpha, a, b, beta, c) -> dict:
 def encode_gemm(ctx: Context, stream, alpha, a, b, beta, c):
     a, b, c = as_view(a), as_view(b), as_view(c)
     check(load().lc_encode_gemm(ctx.h, _stream(stream), float(alpha), a.ref(), b.ref(), float(beta), c.ref()))
+
+
+def encode_gemm_noalloc(ctx: Context, stream, alpha, a, b, beta, c):
+    """encode_gemm with its split-K scratch in fixed per-device arrays (no device allocation).
+    Calls that may run concurrently race on those arrays; the first call on a device does set-up."""
+    a, b, c = as_view(a), as_view(b), as_view(c)
+    check(load().lc_encode_gemm_noalloc(ctx.h, _stream(stream), float(alpha), a.ref(), b.ref(), float(beta), c.ref()))
 
 
 def gemm(ctx: Context, alpha, a, b, beta, c):
