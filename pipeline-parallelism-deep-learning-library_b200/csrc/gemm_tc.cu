@@ -55,14 +55,19 @@ struct KParams {
   float* partial;   // split-K: [splits][batch][M][N] raw partial sums
   int* counters;    // split-K fixup: one arrival counter per (batch, tile, epilogue warp), zero at launch
   int32_t fixup;    // 1: the last-arriving warp reduces in the kernel; 0: a separate reduce kernel does
+  int32_t split_minor;  // unit u = tile * splits + split (CTA pairs); else u = split * tiles + tile
+  int32_t a_once, b_once;  // the operand is read by exactly one CTA (one tile column / row): evict first
   int32_t vec;      // C's columns contiguous and every row start 16-byte aligned (C, aux and aux2)
+  int32_t tvec;     // C's rows contiguous instead (swapped products), runs of 8 rows 16-byte aligned
   int* err;
   const void* aux;
   void* aux2;
   float lr;
 };
 
-template <int BN, bool TF32X3>
+constexpr int kSmemMax = 232448;  // dynamic shared memory a CTA may opt in to on sm_100
+
+template <int BN, bool TF32X3, bool PAIR = false>
 struct Cfg {
   static constexpr int EPR = TF32X3 ? 32 : 64;             // elements per 128-byte row
   static constexpr int BK = EPR;                           // K per stage
@@ -71,7 +76,10 @@ struct Cfg {
   static constexpr int A_BYTES = kBM * kRowBytes;          // 16 KiB
   static constexpr int B_BYTES = BN * kRowBytes;
   static constexpr int STAGE_BYTES = (A_BYTES + B_BYTES) * (TF32X3 ? 2 : 1);
-  static constexpr int STAGES = (TF32X3 ? 196608 : 196608) / STAGE_BYTES;
+  // PAIR: the peer's raw partial of this CTA's column half lands here (f32, 128 x BN/2)
+  static constexpr int RECV_BYTES = PAIR ? kBM * (BN / 2) * 4 : 0;
+  static constexpr int STAGES_FIT = (kSmemMax - 1024 - 512 - RECV_BYTES) / STAGE_BYTES;
+  static constexpr int STAGES = PAIR ? (STAGES_FIT < 8 ? STAGES_FIT : 8) : 196608 / STAGE_BYTES;
   // 2 accumulators (+ the 3xTF32 running sum), rounded up to the power of two tcgen05.alloc takes
   static constexpr int TMEM_NEED = (TF32X3 ? 3 : 2) * BN;
   static constexpr int TMEM_COLS = TMEM_NEED <= 32 ? 32 : TMEM_NEED <= 64 ? 64 : TMEM_NEED <= 128 ? 128
@@ -82,18 +90,28 @@ struct Cfg {
   // for 3xTF32, which bounds the truncation bias of the tensor core's f32 accumulation to
   // about 24 ulp-halves per chunk while the chunks themselves are summed round-to-nearest.
   static constexpr int KC = TF32X3 ? 2 : (1 << 30);
-  static constexpr int BAR_BYTES = 8 * (3 * STAGES + 5) + 16;
-  static constexpr int SMEM = STAGES * STAGE_BYTES + ((BAR_BYTES + 15) / 16) * 16 + 1024;
+  static constexpr int BAR_BYTES = 8 * (3 * STAGES + 7) + 16;
+  static constexpr int SMEM = STAGES * STAGE_BYTES + ((BAR_BYTES + 15) / 16) * 16 + RECV_BYTES + 1024;
   static_assert(STAGES >= 2, "at least two stages");
+  static_assert(SMEM <= kSmemMax, "shared memory budget");
+  static_assert(!PAIR || (!TF32X3 && BN <= 128), "CTA pairs: 16-bit inputs, BN <= 128");
 };
 
 __device__ __forceinline__ void unit_coords(const KParams& p, int32_t u, int32_t* b, int32_t* split, int32_t* tm,
                                             int32_t* tn) {
   const int32_t per = p.tiles_m * p.tiles_n;
-  const int32_t bs = u / per;
-  int32_t t = u - bs * per;
-  *b = bs / p.splits;
-  *split = bs - *b * p.splits;
+  int32_t t;
+  if (p.split_minor) {
+    const int32_t tt = u / p.splits;
+    *split = u - tt * p.splits;
+    *b = tt / per;
+    t = tt - *b * per;
+  } else {
+    const int32_t bs = u / per;
+    t = u - bs * per;
+    *b = bs / p.splits;
+    *split = bs - *b * p.splits;
+  }
   // grouped raster: 8 M tiles share each sweep over N so concurrent CTAs reuse A and B panels in L2
   constexpr int32_t G = 8;
   const int32_t in_group = G * p.tiles_n;
@@ -277,6 +295,87 @@ __device__ __forceinline__ void store_row(const KParams& p, const float (&v)[32]
     if (j < cnt) write_new<EPI>(p, base + (int64_t)j * p.c_ns, v[j], reads ? old[j] : 0.0f);
 }
 
+// Epilogue of a 32-row x 32-column block whose rows are C's contiguous axis (c_ms == 1, the
+// swapped skinny products), from a transposed shared-memory tile: column j's 32 values sit in
+// `slot + j * slot_stride` with row r at position r ^ 4 (j & 7), so groups of 4 rows stay
+// contiguous (16-byte reads) and neither the writes nor the reads conflict on banks.  Lane l
+// handles column (8 * it + l / 4) and rows 8 * (l % 4) .. + 7: one 16-byte access per array
+// for 8 consecutive 16-bit elements (two for f32).  `rows`/`cols`: valid extents.
+template <int EPI>
+__device__ __forceinline__ void store_cols(const KParams& p, const float* slot, int slot_stride, int64_t c_base,
+                                           int32_t rows, int32_t cols) {
+  static_assert(EPI != 2, "the SGD epilogue writes row-contiguous weights");
+  const int lane = threadIdx.x & 31;
+  const int a = lane >> 2, r0 = (lane & 3) * 8;
+  const bool full_rows = r0 + 8 <= rows;
+  const bool reads = EPI == 1 || p.beta != 0.0f;
+  // three passes, so that no shared-memory read waits behind a global store and the global
+  // reads are all in flight together: (1) the tile from shared memory, (2) what the epilogue
+  // reads from C or the mask, (3) compute and store
+  float v[4][8];
+#pragma unroll
+  for (int it = 0; it < 4; it++) {
+    const int j = it * 8 + a;
+    const float4 lo = *reinterpret_cast<const float4*>(slot + j * slot_stride + (r0 ^ (4 * (j & 7))));
+    const float4 hi = *reinterpret_cast<const float4*>(slot + j * slot_stride + ((r0 + 4) ^ (4 * (j & 7))));
+    v[it][0] = lo.x; v[it][1] = lo.y; v[it][2] = lo.z; v[it][3] = lo.w;
+    v[it][4] = hi.x; v[it][5] = hi.y; v[it][6] = hi.z; v[it][7] = hi.w;
+  }
+  float old[4][8];
+#pragma unroll
+  for (int it = 0; it < 4; it++) {
+    const int j = it * 8 + a;
+    const int64_t idx = c_base + (int64_t)j * p.c_ns + r0;
+#pragma unroll
+    for (int e = 0; e < 8; e++) old[it][e] = 0.0f;
+    if (!reads || j >= cols || r0 >= rows) continue;
+    if (!full_rows) {
+      for (int e = 0; e < 8 && r0 + e < rows; e++) old[it][e] = read_old<EPI>(p, idx + e);
+    } else if (EPI == 0 && p.c_dtype == LC_F32) {
+      const float4 o0 = *reinterpret_cast<const float4*>(static_cast<const float*>(p.c) + idx);
+      const float4 o1 = *reinterpret_cast<const float4*>(static_cast<const float*>(p.c) + idx + 4);
+      old[it][0] = o0.x; old[it][1] = o0.y; old[it][2] = o0.z; old[it][3] = o0.w;
+      old[it][4] = o1.x; old[it][5] = o1.y; old[it][6] = o1.z; old[it][7] = o1.w;
+    } else {
+      const uint4 raw = *reinterpret_cast<const uint4*>(
+          static_cast<const uint16_t*>(EPI == 1 ? p.aux : static_cast<const void*>(p.c)) + idx);
+      const uint32_t w4[4] = {raw.x, raw.y, raw.z, raw.w};
+#pragma unroll
+      for (int e = 0; e < 4; e++) {
+        const uint16_t lo = (uint16_t)(w4[e] & 0xffffu), hi = (uint16_t)(w4[e] >> 16);
+        old[it][2 * e] = EPI == 1 ? __uint_as_float((uint32_t)lo << 16) : from_half_bits(p, lo);
+        old[it][2 * e + 1] = EPI == 1 ? __uint_as_float((uint32_t)hi << 16) : from_half_bits(p, hi);
+      }
+    }
+  }
+#pragma unroll
+  for (int it = 0; it < 4; it++) {
+    const int j = it * 8 + a;
+    if (j >= cols || r0 >= rows) continue;
+    const int64_t idx = c_base + (int64_t)j * p.c_ns + r0;
+    float out[8];
+#pragma unroll
+    for (int e = 0; e < 8; e++) {
+      if constexpr (EPI == 0) out[e] = finish(p, v[it][e], old[it][e]);
+      else out[e] = old[it][e] > 0.0f ? __fmul_rn(p.alpha, v[it][e]) : 0.0f;
+    }
+    if (!full_rows) {
+      for (int e = 0; e < 8 && r0 + e < rows; e++) store_c(p, idx + e, out[e]);
+    } else if (p.c_dtype == LC_F32) {
+      float4* dst = reinterpret_cast<float4*>(static_cast<float*>(p.c) + idx);
+      dst[0] = make_float4(out[0], out[1], out[2], out[3]);
+      dst[1] = make_float4(out[4], out[5], out[6], out[7]);
+    } else {
+      uint4 o;
+      o.x = to_half_bits(p, out[0]) | ((uint32_t)to_half_bits(p, out[1]) << 16);
+      o.y = to_half_bits(p, out[2]) | ((uint32_t)to_half_bits(p, out[3]) << 16);
+      o.z = to_half_bits(p, out[4]) | ((uint32_t)to_half_bits(p, out[5]) << 16);
+      o.w = to_half_bits(p, out[6]) | ((uint32_t)to_half_bits(p, out[7]) << 16);
+      *reinterpret_cast<uint4*>(static_cast<uint16_t*>(p.c) + idx) = o;
+    }
+  }
+}
+
 __device__ __forceinline__ float* partial_row(const KParams& p, int32_t split, int32_t b, int32_t m) {
   return p.partial + (((int64_t)split * p.batch + b) * p.M + m) * (int64_t)p.N;
 }
@@ -324,11 +423,11 @@ __device__ __forceinline__ void sum_partials(const KParams& p, float (&v)[32], i
   }
 }
 
-template <int BN, bool TF32X3, int EPI>
-__global__ void __launch_bounds__(Cfg<BN, TF32X3>::THREADS, 1)
+template <int BN, bool TF32X3, int EPI, bool PAIR>
+__global__ void __launch_bounds__(Cfg<BN, TF32X3, PAIR>::THREADS, 1)
     gemm_tc_kernel(const __grid_constant__ CUtensorMap tma_a, const __grid_constant__ CUtensorMap tma_b,
                    const KParams p) {
-  using C = Cfg<BN, TF32X3>;
+  using C = Cfg<BN, TF32X3, PAIR>;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   // ring layout: [A hi][B hi] per stage, then (3xTF32) [A lo][B lo] per stage
@@ -344,7 +443,10 @@ __global__ void __launch_bounds__(Cfg<BN, TF32X3>::THREADS, 1)
   uint64_t* tfull = bars + 3 * C::STAGES;
   uint64_t* tempty = tfull + 2;
   uint64_t* drain = tempty + 2;
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain + 1);
+  uint64_t* recv_full = drain + 1;  // PAIR: the peer's half-tile has landed here (128 arrivals)
+  uint64_t* recv_free = drain + 2;  // PAIR: the peer has consumed what this CTA sent it (128 arrivals)
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain + 3);
+  float* recv = reinterpret_cast<float*>(reinterpret_cast<uint8_t*>(bars) + ((C::BAR_BYTES + 15) / 16) * 16);
 
   const int warp = threadIdx.x / 32;
   const int lane = threadIdx.x & 31;
@@ -360,6 +462,8 @@ __global__ void __launch_bounds__(Cfg<BN, TF32X3>::THREADS, 1)
       lcd::mbar_init(&tempty[a], 128);
     }
     lcd::mbar_init(drain, 1);
+    lcd::mbar_init(recv_full, 128);
+    lcd::mbar_init(recv_free, 128);
     lcd::fence_mbar_init();
   }
   if (warp == 1) {
@@ -374,12 +478,20 @@ __global__ void __launch_bounds__(Cfg<BN, TF32X3>::THREADS, 1)
   __syncthreads();
   lcd::tc_fence_after();
   const uint32_t tmem_base = *tmem_slot;
+  // both CTAs of a pair have initialised their barriers before either arrives on the other's
+  if constexpr (PAIR) lcd::cluster_sync();
+  const uint32_t rank = PAIR ? lcd::cluster_ctarank() : 0u;
+  // Programmatic dependent launch: the next kernel on the stream may start its own set-up now.
+  // Everything below that reads or writes global memory first waits for the previous kernel.
+  lcd::griddep_launch_dependents();
 
   constexpr uint32_t kStageTx = C::A_BYTES + C::B_BYTES;
 
   if (warp == 0) {
     if (lane == 0) {
       // ---------------- TMA producer ----------------
+      lcd::griddep_wait();
+      const uint64_t once = lcd::policy_evict_first();
       int s = 0;
       uint32_t ph = 0;
       uint32_t filled = 0, last_par = 0;  // bit s: stage s filled at least once / parity of its last fill
@@ -396,19 +508,23 @@ __global__ void __launch_bounds__(Cfg<BN, TF32X3>::THREADS, 1)
           }
           lcd::mbar_arrive_expect_tx(&full[s], kStageTx);
           const int32_t k0 = kt * C::BK;
+          auto load = [&](void* dst, const CUtensorMap* map, int32_t c0, int32_t c1, bool hint) {
+            if (hint) lcd::tma_load_3d_hint(dst, map, &full[s], c0, c1, b, once);
+            else lcd::tma_load_3d(dst, map, &full[s], c0, c1, b);
+          };
           if (!p.a_mn) {
-            lcd::tma_load_3d(a_hi(s), &tma_a, &full[s], k0, tm * kBM, b);
+            load(a_hi(s), &tma_a, k0, tm * kBM, p.a_once);
           } else {
 #pragma unroll
             for (int j = 0; j < kBM / C::EPR; j++)
-              lcd::tma_load_3d(a_hi(s) + j * (C::BK * kRowBytes), &tma_a, &full[s], tm * kBM + j * C::EPR, k0, b);
+              load(a_hi(s) + j * (C::BK * kRowBytes), &tma_a, tm * kBM + j * C::EPR, k0, p.a_once);
           }
           if (!p.b_mn) {
-            lcd::tma_load_3d(b_hi(s), &tma_b, &full[s], k0, tn * BN, b);
+            load(b_hi(s), &tma_b, k0, tn * BN, p.b_once);
           } else {
 #pragma unroll
             for (int j = 0; j < BN / C::EPR; j++)
-              lcd::tma_load_3d(b_hi(s) + j * (C::BK * kRowBytes), &tma_b, &full[s], tn * BN + j * C::EPR, k0, b);
+              load(b_hi(s) + j * (C::BK * kRowBytes), &tma_b, tn * BN + j * C::EPR, k0, p.b_once);
           }
           filled |= 1u << s;
           last_par = (last_par & ~(1u << s)) | (ph << s);
@@ -505,9 +621,10 @@ __global__ void __launch_bounds__(Cfg<BN, TF32X3>::THREADS, 1)
     // Warp q owns TMEM lanes (tile rows) 32q..32q+31; lane l holds tile row 32q + l.
     const int q = warp & 3;
     const uint32_t lane_base = tmem_base + ((uint32_t)(q * 32) << 16);
-    const bool split_mode = p.splits > 1;
+    const bool split_mode = p.splits > 1 && !PAIR;
     int32_t h = 0;
     bool ok = true;
+    lcd::griddep_wait();
     for (int32_t u = blockIdx.x; ok && u < p.units; u += gridDim.x) {
       int32_t b, split, tm, tn;
       unit_coords(p, u, &b, &split, &tm, &tn);
@@ -564,6 +681,85 @@ __global__ void __launch_bounds__(Cfg<BN, TF32X3>::THREADS, 1)
           lcd::tmem_ld_wait();
           emit(r, tn * BN + g * 32);
         }
+      } else if constexpr (PAIR) {
+        // CTA pair (cluster of 2) splitting K in halves.  Rank r finalises the column half r of
+        // the tile: each CTA writes the raw accumulator columns of the other half into the
+        // other's receive buffer through distributed shared memory, then adds what it received
+        // to its own half in split order (rank 0's partial first, from +0, as the global split-K
+        // paths sum) and runs the epilogue.  Receive buffer: 128 rows x BN/2 floats, 16-byte
+        // chunk c of row r stored at c ^ (r & 7), so the 32 rows a warp touches at once spread
+        // over all banks.
+        constexpr int HB = BN / 2;   // floats per receive-buffer row
+        constexpr int GH = BN / 64;  // 32-column groups per half
+        const int acc = h & 1;
+        if (!lcd::mbar_wait(&tfull[acc], (h >> 1) & 1, p.err)) break;
+        lcd::tc_fence_after();
+        const int row = q * 32 + lane;
+        const uint32_t sw = (uint32_t)(row & 7);
+        const uint32_t peer = rank ^ 1u;
+        // (1) the peer's half, once the peer has consumed what this CTA sent for the last tile
+        if (!lcd::mbar_wait_cluster(recv_free, (h & 1) ^ 1, p.err)) break;
+        {
+          const uint32_t dst = lcd::mapa_shared(lcd::smem_u32(recv + row * HB), peer);
+          uint32_t r[GH][32];
+#pragma unroll
+          for (int gl = 0; gl < GH; gl++)
+            lcd::tmem_ld_32x32b_x32(lane_base + acc * BN + (peer * GH + gl) * 32, r[gl]);
+          lcd::tmem_ld_wait();
+#pragma unroll
+          for (int gl = 0; gl < GH; gl++) {
+#pragma unroll
+            for (int k = 0; k < 8; k++) {
+              const uint32_t chunk = (uint32_t)(gl * 8) + ((uint32_t)k ^ sw);
+              lcd::st_cluster_v4(dst + chunk * 16, __uint_as_float(r[gl][4 * k]), __uint_as_float(r[gl][4 * k + 1]),
+                                 __uint_as_float(r[gl][4 * k + 2]), __uint_as_float(r[gl][4 * k + 3]));
+            }
+          }
+        }
+        lcd::mbar_arrive_remote(lcd::mapa_shared(lcd::smem_u32(recv_full), peer));
+        // (2) this CTA's half: its own accumulator plus the peer's, then the epilogue
+        if (!lcd::mbar_wait_cluster(recv_full, h & 1, p.err)) break;
+        const float* src = recv + row * HB;
+#pragma unroll 1
+        for (int gl = 0; gl < GH; gl++) {
+          const int g = (int)rank * GH + gl;
+          uint32_t r[32];
+          lcd::tmem_ld_32x32b_x32(lane_base + acc * BN + g * 32, r);
+          lcd::tmem_ld_wait();
+          float v[32];
+#pragma unroll
+          for (int k = 0; k < 8; k++) {
+            const uint32_t chunk = (uint32_t)(gl * 8) + ((uint32_t)k ^ sw);
+            const float4 o = *reinterpret_cast<const float4*>(src + chunk * 4);
+            const float in[4] = {o.x, o.y, o.z, o.w};
+#pragma unroll
+            for (int e = 0; e < 4; e++) {
+              const float mine = __uint_as_float(r[4 * k + e]);
+              v[4 * k + e] = rank == 0 ? __fadd_rn(__fadd_rn(0.0f, mine), in[e]) : __fadd_rn(__fadd_rn(0.0f, in[e]), mine);
+            }
+          }
+          const int32_t n0 = tn * BN + g * 32;
+          const int32_t cnt = min(32, p.N - n0);
+          if (p.tvec) {
+            // transpose through this warp's rows of the receive buffer (group gl's 128 bytes of
+            // each row, read above by every lane: hence the first __syncwarp): column j's 32
+            // values go to row j of the area, row r at position r ^ 4 (j & 7)
+            float* slot = recv + (q * 32) * HB + gl * 32;
+            __syncwarp();
+#pragma unroll
+            for (int j = 0; j < 32; j++) slot[j * HB + (lane ^ (4 * (j & 7)))] = v[j];
+            __syncwarp();
+            const int32_t mw = tm * kBM + q * 32;
+            store_cols<EPI>(p, slot, HB, p.c_off + (int64_t)b * p.c_bs + mw + (int64_t)n0 * p.c_ns,
+                            min(32, p.M - mw), cnt);
+          } else if (m < p.M && cnt > 0) {
+            store_row<EPI>(p, v, c_row + (int64_t)n0 * p.c_ns, cnt);
+          }
+        }
+        lcd::mbar_arrive_remote(lcd::mapa_shared(lcd::smem_u32(recv_free), peer));
+        lcd::tc_fence_before();
+        lcd::mbar_arrive(&tempty[acc]);
+        h++;
       } else {
         const int acc = h & 1;
         if (!lcd::mbar_wait(&tfull[acc], (h >> 1) & 1, p.err)) break;
@@ -665,6 +861,8 @@ __global__ void __launch_bounds__(Cfg<BN, TF32X3>::THREADS, 1)
     lcd::tc_fence_after();
     lcd::tmem_dealloc(tmem_base, C::TMEM_COLS);
   }
+  // neither CTA of a pair leaves while the other may still access its shared memory
+  if constexpr (PAIR) lcd::cluster_sync();
 }
 
 // ---- split-K reduce for many splits: C = epilogue(sum_s partial[s]), splits summed in order -----
@@ -815,21 +1013,79 @@ lc_status make_map(CUtensorMap* map, const void* base, int in_dtype, uint64_t in
   return LC_OK;
 }
 
-template <int BN, bool TF32X3, int EPI>
-lc_status launch_kernel(lc_context* ctx, cudaStream_t s, const CUtensorMap& ta, const CUtensorMap& tb, const KParams& p,
-                        int grid) {
-  using C = Cfg<BN, TF32X3>;
+template <int BN, bool TF32X3, int EPI, bool PAIR>
+cudaLaunchConfig_t launch_config(cudaStream_t s, int grid, cudaLaunchAttribute (&at)[2]) {
+  using C = Cfg<BN, TF32X3, PAIR>;
+  cudaLaunchConfig_t cfg{};
+  cfg.gridDim = dim3((unsigned)grid);
+  cfg.blockDim = dim3(C::THREADS);
+  cfg.dynamicSmemBytes = C::SMEM;
+  cfg.stream = s;
+  int na = 0;
+  // programmatic dependent launch: this grid's set-up may overlap the previous kernel's tail
+  at[na].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  at[na].val.programmaticStreamSerializationAllowed = 1;
+  na++;
+  if (PAIR) {
+    at[na].id = cudaLaunchAttributeClusterDimension;
+    at[na].val.clusterDim.x = 2;
+    at[na].val.clusterDim.y = 1;
+    at[na].val.clusterDim.z = 1;
+    na++;
+  }
+  cfg.attrs = at;
+  cfg.numAttrs = na;
+  return cfg;
+}
+
+template <int BN, bool TF32X3, int EPI, bool PAIR>
+lc_status prepare_kernel(lc_context* ctx) {
+  using C = Cfg<BN, TF32X3, PAIR>;
   static bool attr_set[64] = {false};
-  auto kern = gemm_tc_kernel<BN, TF32X3, EPI>;
   if (!attr_set[ctx->device % 64]) {
-    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM);
+    cudaError_t e = cudaFuncSetAttribute(gemm_tc_kernel<BN, TF32X3, EPI, PAIR>,
+                                         cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM);
     if (e != cudaSuccess) return lc::cuda_fail(e, "cudaFuncSetAttribute(gemm)");
     attr_set[ctx->device % 64] = true;
   }
-  kern<<<grid, C::THREADS, C::SMEM, s>>>(ta, tb, p);
-  lc::record_launch(ctx, TF32X3 ? (BN == 64 ? "gemm_tf32x3_n64" : "gemm_tf32x3_n128")
-                                : (BN == 64 ? "gemm_bf16_n64" : BN == 128 ? "gemm_bf16_n128" : "gemm_bf16_n256"));
-  cudaError_t e = cudaGetLastError();
+  return LC_OK;
+}
+
+// How many CTA pairs of this kernel fit on the device at once (0 when pairs cannot launch).
+template <int BN, int EPI>
+int pair_capacity(lc_context* ctx) {
+  static int cap[64];
+  static bool known[64] = {false};
+  const int d = ctx->device % 64;
+  if (!known[d]) {
+    int n = 0;
+    if (prepare_kernel<BN, false, EPI, true>(ctx) == LC_OK) {
+      cudaLaunchAttribute at[2];
+      cudaLaunchConfig_t cfg = launch_config<BN, false, EPI, true>(nullptr, 2, at);
+      if (cudaOccupancyMaxActiveClusters(&n, gemm_tc_kernel<BN, false, EPI, true>, &cfg) != cudaSuccess) {
+        cudaGetLastError();
+        n = 0;
+      }
+    }
+    cap[d] = n;
+    known[d] = true;
+  }
+  return cap[d];
+}
+
+template <int BN, bool TF32X3, int EPI, bool PAIR>
+lc_status launch_kernel(lc_context* ctx, cudaStream_t s, const CUtensorMap& ta, const CUtensorMap& tb, const KParams& p,
+                        int grid) {
+  lc_status st = prepare_kernel<BN, TF32X3, EPI, PAIR>(ctx);
+  if (st) return st;
+  cudaLaunchAttribute at[2];
+  cudaLaunchConfig_t cfg = launch_config<BN, TF32X3, EPI, PAIR>(s, grid, at);
+  cudaError_t e = cudaLaunchKernelEx(&cfg, gemm_tc_kernel<BN, TF32X3, EPI, PAIR>, ta, tb, p);
+  lc::record_launch(ctx, PAIR ? (BN == 64 ? "gemm_bf16_pair_n64" : "gemm_bf16_pair_n128")
+                         : TF32X3 ? (BN == 64 ? "gemm_tf32x3_n64" : "gemm_tf32x3_n128")
+                                  : (BN == 64 ? "gemm_bf16_n64" : BN == 128 ? "gemm_bf16_n128" : "gemm_bf16_n256"));
+  if (e != cudaSuccess) return lc::cuda_fail(e, "gemm launch");
+  e = cudaGetLastError();
   if (e != cudaSuccess) return lc::cuda_fail(e, "gemm launch");
   return LC_OK;
 }
@@ -909,6 +1165,19 @@ lc_status gemm_run(lc_context* ctx, cudaStream_t s, const GemmProblem& pr, lc_co
   kps = ceil_div(k_tiles, splits);
   splits = ceil_div(k_tiles, kps);
   const int64_t units = tiles * splits;
+  // A 2-way split of 16-bit inputs runs as CTA pairs (clusters of 2) that reduce through
+  // distributed shared memory: no partial sums in global memory, no second pass.
+  static const bool env_no_pair = [] {
+    const char* e = getenv("LC_GEMM_PAIRS");  // tuning override: "0" keeps 2-way splits in global memory
+    return e != nullptr && e[0] == '0';
+  }();
+  int64_t pair_clusters = 0;
+  if (!dry_run && !tf32x3 && splits == 2 && bn <= 128 && pr.epi != 2 && !env_no_pair) {
+    const int cap = bn == 64 ? (pr.epi == 0 ? pair_capacity<64, 0>(ctx) : pair_capacity<64, 1>(ctx))
+                             : (pr.epi == 0 ? pair_capacity<128, 0>(ctx) : pair_capacity<128, 1>(ctx));
+    pair_clusters = std::min<int64_t>({tiles, (int64_t)cap, (ctx->sm_count - pr.reserve_sms) / 2});
+  }
+  const bool pair = pair_clusters > 0;
   if (units >= (1ll << 31) || k_tiles >= (1ll << 31)) return fail(LC_ERR_INVALID_ARGUMENT, "problem too large");
 
   if (operand_major(A) < 0 || operand_major(B) < 0) return fail(LC_ERR_INVALID_ARGUMENT, "operand has no unit stride");
@@ -961,6 +1230,13 @@ lc_status gemm_run(lc_context* ctx, cudaStream_t s, const GemmProblem& pr, lc_co
   p.tiles_m = (int32_t)tiles_m;
   p.tiles_n = (int32_t)tiles_n;
   p.units = (int32_t)units;
+  p.split_minor = pair ? 1 : 0;
+  static const bool env_no_hint = [] {
+    const char* e = getenv("LC_GEMM_EVICT_FIRST");  // tuning override: "0" drops the streaming hint
+    return e != nullptr && e[0] == '0';
+  }();
+  p.a_once = (tiles_n == 1 && !env_no_hint) ? 1 : 0;
+  p.b_once = (tiles_m == 1 && !env_no_hint) ? 1 : 0;
   p.a_mn = a_mn;
   p.b_mn = b_mn;
   const uint32_t fmt = tf32x3 ? 2u : (pr.in_dtype == LC_BF16 ? 1u : 0u);
@@ -984,6 +1260,8 @@ lc_status gemm_run(lc_context* ctx, cudaStream_t s, const GemmProblem& pr, lc_co
     const bool strides8 = (p.c_off % 8) == 0 && (p.c_ms % 8) == 0 && (pr.batch == 1 || (p.c_bs % 8) == 0);
     const bool ptrs = pr.epi == 0 ? al16(pr.c) : pr.epi == 1 ? al16(pr.c) && al16(pr.aux) : al16(pr.aux) && al16(pr.aux2);
     p.vec = (c_ns == 1 && strides8 && ptrs) ? 1 : 0;
+    const bool tstrides8 = (p.c_off % 8) == 0 && (p.c_ns % 8) == 0 && (pr.batch == 1 || (p.c_bs % 8) == 0);
+    p.tvec = (c_ms == 1 && c_ns != 1 && tstrides8 && ptrs && pr.epi != 2) ? 1 : 0;
   }
   p.aux = pr.aux;
   p.aux2 = pr.aux2;
@@ -995,7 +1273,7 @@ lc_status gemm_run(lc_context* ctx, cudaStream_t s, const GemmProblem& pr, lc_co
   // the stream-ordered pool, counters zeroed in stream order.
   constexpr int64_t kFixupMaxSplits = 4;
   void* scratch = nullptr;
-  if (splits > 1) {
+  if (splits > 1 && !pair) {
     p.fixup = splits <= kFixupMaxSplits ? 1 : 0;
     const size_t part_bytes = sizeof(float) * (size_t)splits * pr.batch * M * N;
     const size_t part_pad = (part_bytes + 255) / 256 * 256;
@@ -1051,22 +1329,28 @@ lc_status gemm_run(lc_context* ctx, cudaStream_t s, const GemmProblem& pr, lc_co
       }
     }
   }
-  const int grid = (int)std::max<int64_t>(1, std::min<int64_t>(units, ctx->sm_count - pr.reserve_sms));
-  if (tf32x3) {
-    st = bn == 64 ? launch_kernel<64, true, 0>(ctx, s, ta, tb, p, grid)
-                  : launch_kernel<128, true, 0>(ctx, s, ta, tb, p, grid);
+  const int grid = pair ? (int)(2 * pair_clusters)
+                        : (int)std::max<int64_t>(1, std::min<int64_t>(units, ctx->sm_count - pr.reserve_sms));
+  if (pair) {
+    st = bn == 64 ? (pr.epi == 0 ? launch_kernel<64, false, 0, true>(ctx, s, ta, tb, p, grid)
+                                 : launch_kernel<64, false, 1, true>(ctx, s, ta, tb, p, grid))
+                  : (pr.epi == 0 ? launch_kernel<128, false, 0, true>(ctx, s, ta, tb, p, grid)
+                                 : launch_kernel<128, false, 1, true>(ctx, s, ta, tb, p, grid));
+  } else if (tf32x3) {
+    st = bn == 64 ? launch_kernel<64, true, 0, false>(ctx, s, ta, tb, p, grid)
+                  : launch_kernel<128, true, 0, false>(ctx, s, ta, tb, p, grid);
   } else {
     auto by_bn = [&](auto epi_tag) {
       constexpr int E = decltype(epi_tag)::value;
-      return bn == 64    ? launch_kernel<64, false, E>(ctx, s, ta, tb, p, grid)
-             : bn == 128 ? launch_kernel<128, false, E>(ctx, s, ta, tb, p, grid)
-                         : launch_kernel<256, false, E>(ctx, s, ta, tb, p, grid);
+      return bn == 64    ? launch_kernel<64, false, E, false>(ctx, s, ta, tb, p, grid)
+             : bn == 128 ? launch_kernel<128, false, E, false>(ctx, s, ta, tb, p, grid)
+                         : launch_kernel<256, false, E, false>(ctx, s, ta, tb, p, grid);
     };
     st = pr.epi == 0   ? by_bn(std::integral_constant<int, 0>{})
          : pr.epi == 1 ? by_bn(std::integral_constant<int, 1>{})
                        : by_bn(std::integral_constant<int, 2>{});
   }
-  if (st == LC_OK && splits > 1 && !p.fixup) {
+  if (st == LC_OK && splits > 1 && !pair && !p.fixup) {
     const int64_t quads = (int64_t)pr.batch * M * ((N + 3) / 4);
     const int rgrid = (int)std::max<int64_t>(1, std::min<int64_t>(ceil_div(quads, 256), (int64_t)ctx->sm_count * 8));
     if (pr.epi == 0) splitk_reduce_kernel<0><<<rgrid, 256, 0, s>>>(p);
