@@ -140,7 +140,7 @@ def run_reference(args):
     line = {
         "impl": "reference", "metric": METRIC, "value": value, "unit": "samples/s", "n_gpus": args.gpus,
         "steps": args.steps, "warmup": args.warmup, "ms_per_step": 1000.0 * BATCH / value, "higher_is_better": True,
-        "scaling": "weak", "vs_baseline": None, "dtype": "bf16 in, f32 accumulate", "data": "synthetic",
+        "scaling": "strong", "vs_baseline": None, "dtype": "bf16 in, f32 accumulate", "data": "synthetic",
         "config": {"workload": WORKLOAD, "layers": LAYERS, "width": WIDTH, "global_batch": BATCH,
                    "microbatch": MB, "microbatches": MBS, "parallelism": f"pp{args.gpus}"},
         "cpu_baseline": {"value": value, "unit": "samples/s", "cores": threads, "kind": "port",
@@ -412,7 +412,7 @@ def main():
             cpu_v, cpu_s = cpu_sample(1)
         line = {
             "metric": METRIC, "value": value, "unit": "samples/s", "n_gpus": world, "steps": args.steps,
-            "warmup": args.warmup, "ms_per_step": ms / args.steps, "higher_is_better": True, "scaling": "weak",
+            "warmup": args.warmup, "ms_per_step": ms / args.steps, "higher_is_better": True, "scaling": "strong",
             "vs_baseline": None, "dtype": "bf16", "data": "synthetic (seeded SplitMix64 N(0,1) inputs/targets, "
                                                           "N(0,1/8192) weights on device)",
             "config": {"workload": WORKLOAD, "layers": LAYERS, "width": WIDTH, "global_batch": BATCH,
