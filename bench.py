@@ -245,6 +245,11 @@ def op_figures(hbm_peak, tc_peak):
     return out
 
 
+# dram__bytes_read.sum + dram__bytes_write.sum of one launch of the forward product, from the ncu
+# capture summarised in profiles/gemm_bf16_pair_n64_fwd_64x8192x8192.md (135.37 MB + 4.77 MB)
+TRAFFIC_FWD_GEMM = 140_140_544
+
+
 def forward_gemm_roofline(hbm_peak):
     """The step's dominant kernel: the forward/dgrad GEMM [64, 8192] x [8192, 8192] bf16 that
     streams one weight matrix from HBM.  Timed alone with CUDA events on its launch stream."""
@@ -270,7 +275,9 @@ def forward_gemm_roofline(hbm_peak):
     ctx.close()
     torch.cuda.empty_cache()
     return {"bound": "hbm", "achieved": achieved, "peak": hbm_peak, "unit": "GB/s", "frac": achieved / hbm_peak,
-            "traffic": None, "kernel": "gemm_bf16_n64 (+split-K reduce), forward/dgrad shape [64,8192]x[8192,8192]",
+            "traffic": TRAFFIC_FWD_GEMM,
+            "kernel": "gemm_tc_kernel<BN=64, bf16, pair> (K split over a CTA pair, reduced through distributed "
+                      "shared memory), forward/dgrad shape [64,8192]x[8192,8192]",
             "algorithmic_bytes_per_launch": algo_bytes, "ms_per_launch": ms}
 
 
