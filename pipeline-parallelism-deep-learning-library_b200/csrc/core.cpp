@@ -255,6 +255,7 @@ lc_status lc_context_destroy(lc_context* ctx) {
   cudaStreamSynchronize(ctx->stream);
   if (ctx->split_part) cudaFree(ctx->split_part);
   if (ctx->split_cnt) cudaFree(ctx->split_cnt);
+  if (ctx->chain_cnt) cudaFree(ctx->chain_cnt);
   cudaFree(ctx->d_error);
   cudaStreamDestroy(ctx->stream);
   delete ctx;

@@ -63,6 +63,18 @@ bool tma_operand_ok(const GemmOperand& o, int in_dtype);
 // tma_operand_ok.  With dry_run only `plan` is filled.
 lc_status gemm_run(lc_context* ctx, cudaStream_t s, const GemmProblem& p, lc_contract_plan* plan, bool dry_run);
 
+// A chain of dependent skinny products (product l + 1 reads what product l writes) in one
+// cooperative launch whose CTAs stay resident across the chain.  Each product must plan as a
+// 2-way split run by CTA pairs with BN = 64 and all must share one epilogue; otherwise nothing
+// is launched and *chained is false (the caller runs the products one by one).  `a_stable`:
+// no kernel that may still be running writes any A operand (the weights), so the next
+// product's A tiles load ahead of the previous product's completion.  Results are bit-identical
+// to launching the products one at a time with gemm_run.
+// `max_clusters` (> 0) caps the CTA pairs, leaving the rest of the SMs to work on another
+// stream (each pair then takes several tiles of a product).
+lc_status gemm_chain_run(lc_context* ctx, cudaStream_t s, const GemmProblem* probs, int n, bool a_stable,
+                         int max_clusters, bool* chained);
+
 // lc_encode_gemm's planning and launch with split-K scratch supplied by the caller: refuses
 // products whose operands would need staging copies, or whose split does not fit the scratch.
 lc_status gemm_fixed_scratch(lc_context* ctx, void* stream, float alpha, const lc_view* a, const lc_view* b, float beta,

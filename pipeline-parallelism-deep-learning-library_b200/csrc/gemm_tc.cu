@@ -25,6 +25,7 @@
 
 #include <algorithm>
 #include <cstring>
+#include <memory>
 #include <mutex>
 #include <string>
 #include <type_traits>
@@ -91,7 +92,9 @@ struct Cfg {
   // about 24 ulp-halves per chunk while the chunks themselves are summed round-to-nearest.
   static constexpr int KC = TF32X3 ? 2 : (1 << 30);
   static constexpr int BAR_BYTES = 8 * (3 * STAGES + 7) + 16;
-  static constexpr int SMEM = STAGES * STAGE_BYTES + ((BAR_BYTES + 15) / 16) * 16 + RECV_BYTES + 1024;
+  // non-pair kernels: one 32 x 36 f32 tile per epilogue warp for coalesced row stores
+  static constexpr int EPI_STAGE_BYTES = PAIR ? 0 : 4 * 32 * 36 * 4;
+  static constexpr int SMEM = STAGES * STAGE_BYTES + ((BAR_BYTES + 15) / 16) * 16 + RECV_BYTES + EPI_STAGE_BYTES + 1024;
   static_assert(STAGES >= 2, "at least two stages");
   static_assert(SMEM <= kSmemMax, "shared memory budget");
   static_assert(!PAIR || (!TF32X3 && BN <= 128), "CTA pairs: 16-bit inputs, BN <= 128");
@@ -376,6 +379,100 @@ __device__ __forceinline__ void store_cols(const KParams& p, const float* slot, 
   }
 }
 
+// Coalesced epilogue of a warp's 32 rows x 32 columns when C's columns are contiguous: lane l
+// holds row l of the block in v[].  The block goes through the warp's shared tile (rows 36
+// floats apart, so 16-byte writes and reads are conflict-free) and comes back with lane l on
+// row 4i + l/8, columns 4(l%8) .. + 3: every global access covers 4 rows x 32 columns, 4 lines
+// (f32) or 4 half-lines (16-bit), instead of one line per lane.  A store pattern with 32 lines
+// per instruction costs the LSU about 5 cycles a line, which made row-per-lane epilogues the
+// bottleneck of the fused-SGD weight gradient.  RAW: store the raw f32 values to `raw` (row
+// stride `raw_ld`, the split-K partials) instead of running the epilogue at C index `base`.
+template <int EPI, bool RAW>
+__device__ __forceinline__ void store_tile32(const KParams& p, const float (&v)[32], float* stage, int64_t base,
+                                             float* raw, int64_t raw_ld, int32_t rows) {
+  const int lane = threadIdx.x & 31;
+  __syncwarp();  // the previous block has been read out of the tile
+  float4* mine = reinterpret_cast<float4*>(stage + lane * 36);
+#pragma unroll
+  for (int k = 0; k < 8; k++) mine[k] = make_float4(v[4 * k], v[4 * k + 1], v[4 * k + 2], v[4 * k + 3]);
+  __syncwarp();
+  const int rr = lane >> 3, cc = (lane & 7) * 4;
+  float x[8][4];
+#pragma unroll
+  for (int i = 0; i < 8; i++) {
+    const float4 t = *reinterpret_cast<const float4*>(stage + (4 * i + rr) * 36 + cc);
+    x[i][0] = t.x;
+    x[i][1] = t.y;
+    x[i][2] = t.z;
+    x[i][3] = t.w;
+  }
+  if constexpr (RAW) {
+#pragma unroll
+    for (int i = 0; i < 8; i++)
+      if (4 * i + rr < rows)
+        *reinterpret_cast<float4*>(raw + (int64_t)(4 * i + rr) * raw_ld + cc) = make_float4(x[i][0], x[i][1], x[i][2], x[i][3]);
+    return;
+  } else {
+    // the values the epilogue reads (C for beta, the mask, the master weights), all in flight together
+    float o[8][4];
+    const bool reads = EPI != 0 || p.beta != 0.0f;
+#pragma unroll
+    for (int i = 0; i < 8; i++) {
+#pragma unroll
+      for (int e = 0; e < 4; e++) o[i][e] = 0.0f;
+      if (!reads || 4 * i + rr >= rows) continue;
+      const int64_t idx = base + (int64_t)(4 * i + rr) * p.c_ms + cc;
+      if (EPI == 2) {
+        // the master weights stream through once: evict-first, so that they do not push the
+        // product's operands out of L2
+        const float4 t = __ldcs(reinterpret_cast<const float4*>(static_cast<const float*>(p.aux) + idx));
+        o[i][0] = t.x;
+        o[i][1] = t.y;
+        o[i][2] = t.z;
+        o[i][3] = t.w;
+      } else if (EPI == 0 && p.c_dtype == LC_F32) {
+        const float4 t = *reinterpret_cast<const float4*>(static_cast<const float*>(p.c) + idx);
+        o[i][0] = t.x;
+        o[i][1] = t.y;
+        o[i][2] = t.z;
+        o[i][3] = t.w;
+      } else {
+        const uint2 t = *reinterpret_cast<const uint2*>(
+            static_cast<const uint16_t*>(EPI == 1 ? p.aux : static_cast<const void*>(p.c)) + idx);
+        const uint16_t h[4] = {(uint16_t)(t.x & 0xffffu), (uint16_t)(t.x >> 16), (uint16_t)(t.y & 0xffffu),
+                               (uint16_t)(t.y >> 16)};
+#pragma unroll
+        for (int e = 0; e < 4; e++) o[i][e] = EPI == 1 ? __uint_as_float((uint32_t)h[e] << 16) : from_half_bits(p, h[e]);
+      }
+    }
+#pragma unroll
+    for (int i = 0; i < 8; i++) {
+      if (4 * i + rr >= rows) continue;
+      const int64_t idx = base + (int64_t)(4 * i + rr) * p.c_ms + cc;
+      float out[4];
+#pragma unroll
+      for (int e = 0; e < 4; e++) {
+        if constexpr (EPI == 0) out[e] = finish(p, x[i][e], o[i][e]);
+        else if constexpr (EPI == 1) out[e] = o[i][e] > 0.0f ? __fmul_rn(p.alpha, x[i][e]) : 0.0f;
+        else out[e] = __fsub_rn(o[i][e], __fmul_rn(p.lr, __fmul_rn(p.alpha, x[i][e])));
+      }
+      if constexpr (EPI == 2) {
+        __stcs(reinterpret_cast<float4*>(static_cast<float*>(const_cast<void*>(p.aux)) + idx),
+               make_float4(out[0], out[1], out[2], out[3]));
+        __stcs(reinterpret_cast<uint2*>(static_cast<uint16_t*>(p.aux2) + idx),
+               make_uint2(f32_to_bf16_rne(out[0]) | ((uint32_t)f32_to_bf16_rne(out[1]) << 16),
+                          f32_to_bf16_rne(out[2]) | ((uint32_t)f32_to_bf16_rne(out[3]) << 16)));
+      } else if (p.c_dtype == LC_F32) {
+        *reinterpret_cast<float4*>(static_cast<float*>(p.c) + idx) = make_float4(out[0], out[1], out[2], out[3]);
+      } else {
+        *reinterpret_cast<uint2*>(static_cast<uint16_t*>(p.c) + idx) =
+            make_uint2(to_half_bits(p, out[0]) | ((uint32_t)to_half_bits(p, out[1]) << 16),
+                       to_half_bits(p, out[2]) | ((uint32_t)to_half_bits(p, out[3]) << 16));
+      }
+    }
+  }
+}
+
 __device__ __forceinline__ float* partial_row(const KParams& p, int32_t split, int32_t b, int32_t m) {
   return p.partial + (((int64_t)split * p.batch + b) * p.M + m) * (int64_t)p.N;
 }
@@ -423,11 +520,74 @@ __device__ __forceinline__ void sum_partials(const KParams& p, float (&v)[32], i
   }
 }
 
-template <int BN, bool TF32X3, int EPI, bool PAIR>
-__global__ void __launch_bounds__(Cfg<BN, TF32X3, PAIR>::THREADS, 1)
-    gemm_tc_kernel(const __grid_constant__ CUtensorMap tma_a, const __grid_constant__ CUtensorMap tma_b,
-                   const KParams p) {
+// ---- where a kernel's products come from ------------------------------------------------------
+// OneProduct: the tensor maps and parameters of a single product, passed as kernel arguments.
+// ChainParams/ChainSrc: a chain of dependent products in one launch (product l + 1 reads what
+// product l writes), for the pipeline's per-microbatch layer loops; CTAs stay resident across
+// the chain and meet at a counter per product instead of a kernel boundary.
+struct OneProduct {
+  const CUtensorMap* a;
+  const CUtensorMap* b;
+  const KParams* p;
+  __device__ __forceinline__ int layers() const { return 1; }
+  __device__ __forceinline__ const KParams& kp(int) const { return *p; }
+  __device__ __forceinline__ const CUtensorMap* map_a(int) const { return a; }
+  __device__ __forceinline__ const CUtensorMap* map_b(int) const { return b; }
+  __device__ __forceinline__ int* counters() const { return nullptr; }
+  __device__ __forceinline__ bool a_stable() const { return false; }
+};
+
+constexpr int kMaxChain = 32;
+
+struct ChainParams {
+  CUtensorMap a[kMaxChain];
+  CUtensorMap b[kMaxChain];
+  KParams p[kMaxChain];
+  int32_t n;
+  int32_t a_stable;  // no kernel that may still be running writes any A operand (the weights)
+  int* counters;     // [n], zero at launch: CTAs whose epilogue finished product l
+};
+
+struct ChainSrc {
+  const ChainParams* cp;
+  __device__ __forceinline__ int layers() const { return cp->n; }
+  // by value: read once per product, not re-read from the parameter block inside the loops
+  __device__ __forceinline__ KParams kp(int l) const { return cp->p[l]; }
+  __device__ __forceinline__ const CUtensorMap* map_a(int l) const { return &cp->a[l]; }
+  __device__ __forceinline__ const CUtensorMap* map_b(int l) const { return &cp->b[l]; }
+  __device__ __forceinline__ int* counters() const { return cp->counters; }
+  __device__ __forceinline__ bool a_stable() const { return cp->a_stable != 0; }
+};
+
+__device__ __forceinline__ int ld_acquire_gpu(const int* p) {
+  int v;
+  asm volatile("ld.acquire.gpu.global.b32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+  return v;
+}
+
+// Bounded wait until *counter >= target (every CTA's epilogue finished the previous product),
+// then orders those generic-proxy writes before this thread's TMA (async-proxy) reads.
+__device__ __forceinline__ bool wait_counter(const int* counter, int target, int* err) {
+  const uint64_t t0 = lcd::global_ns();
+  for (uint32_t i = 0;; ++i) {
+    if (ld_acquire_gpu(counter) >= target) break;
+    __nanosleep(32);  // 128 pollers of one line: leave the L2 some room for the arrivals
+    if ((i & 63u) == 63u) {
+      if (*(volatile int*)err != 0) return false;
+      if (lcd::global_ns() - t0 > lcd::kWaitLimitNs) {
+        atomicOr(err, 1);
+        return false;
+      }
+    }
+  }
+  asm volatile("fence.proxy.async.global;" ::: "memory");
+  return true;
+}
+
+template <int BN, bool TF32X3, int EPI, bool PAIR, class Src>
+__device__ __forceinline__ void gemm_body(const Src& src) {
   using C = Cfg<BN, TF32X3, PAIR>;
+  int* const err = src.kp(0).err;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   // ring layout: [A hi][B hi] per stage, then (3xTF32) [A lo][B lo] per stage
@@ -446,7 +606,9 @@ __global__ void __launch_bounds__(Cfg<BN, TF32X3, PAIR>::THREADS, 1)
   uint64_t* recv_full = drain + 1;  // PAIR: the peer's half-tile has landed here (128 arrivals)
   uint64_t* recv_free = drain + 2;  // PAIR: the peer has consumed what this CTA sent it (128 arrivals)
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain + 3);
+  uint32_t* layer_done = tmem_slot + 1;  // chain: epilogue warps done with their products so far
   float* recv = reinterpret_cast<float*>(reinterpret_cast<uint8_t*>(bars) + ((C::BAR_BYTES + 15) / 16) * 16);
+  float* epi_stage = recv + C::RECV_BYTES / 4;  // non-pair kernels: 4 x (32 x 36) f32
 
   const int warp = threadIdx.x / 32;
   const int lane = threadIdx.x & 31;
@@ -464,6 +626,7 @@ __global__ void __launch_bounds__(Cfg<BN, TF32X3, PAIR>::THREADS, 1)
     lcd::mbar_init(drain, 1);
     lcd::mbar_init(recv_full, 128);
     lcd::mbar_init(recv_free, 128);
+    *layer_done = 0;
     lcd::fence_mbar_init();
   }
   if (warp == 1) {
@@ -471,8 +634,10 @@ __global__ void __launch_bounds__(Cfg<BN, TF32X3, PAIR>::THREADS, 1)
     lcd::tmem_relinquish();
   }
   if (warp == 0 && lane == 0) {
-    lcd::tma_prefetch_desc(&tma_a);
-    lcd::tma_prefetch_desc(&tma_b);
+    for (int l = 0; l < src.layers(); l++) {
+      lcd::tma_prefetch_desc(src.map_a(l));
+      lcd::tma_prefetch_desc(src.map_b(l));
+    }
   }
   lcd::tc_fence_before();
   __syncthreads();
@@ -490,53 +655,103 @@ __global__ void __launch_bounds__(Cfg<BN, TF32X3, PAIR>::THREADS, 1)
   if (warp == 0) {
     if (lane == 0) {
       // ---------------- TMA producer ----------------
-      lcd::griddep_wait();
+      // Each product's loads are gated on what produced its inputs: the previous kernel for the
+      // first product (programmatic dependent launch), the previous product's counter inside a
+      // chain.  When the A operands are stable (weights nobody is writing), A is loaded ahead of
+      // the gate into up to STAGES slots and only the B loads wait.
       const uint64_t once = lcd::policy_evict_first();
+      const uint64_t keep = lcd::policy_evict_last();
       int s = 0;
       uint32_t ph = 0;
       uint32_t filled = 0, last_par = 0;  // bit s: stage s filled at least once / parity of its last fill
       bool ok = true;
-      for (int32_t u = blockIdx.x; ok && u < p.units; u += gridDim.x) {
-        int32_t b, split, tm, tn;
-        unit_coords(p, u, &b, &split, &tm, &tn);
-        const int32_t kb = split * p.kt_per_split;
-        const int32_t ke = min(kb + p.kt_per_split, p.k_tiles);
-        for (int32_t kt = kb; kt < ke; kt++) {
-          if (!lcd::mbar_wait(&empty[s], ph ^ 1u, p.err)) {
-            ok = false;
-            break;
+      for (int l = 0; ok && l < src.layers(); l++) {
+        decltype(auto) p = src.kp(l);  // a chain's are copied to registers once per product
+        const CUtensorMap* ta = src.map_a(l);
+        const CUtensorMap* tb = src.map_b(l);
+        auto gate = [&]() -> bool {
+          if (l == 0) {
+            lcd::griddep_wait();
+            return true;
           }
-          lcd::mbar_arrive_expect_tx(&full[s], kStageTx);
-          const int32_t k0 = kt * C::BK;
-          auto load = [&](void* dst, const CUtensorMap* map, int32_t c0, int32_t c1, bool hint) {
-            if (hint) lcd::tma_load_3d_hint(dst, map, &full[s], c0, c1, b, once);
-            else lcd::tma_load_3d(dst, map, &full[s], c0, c1, b);
-          };
-          if (!p.a_mn) {
-            load(a_hi(s), &tma_a, k0, tm * kBM, p.a_once);
-          } else {
-#pragma unroll
-            for (int j = 0; j < kBM / C::EPR; j++)
-              load(a_hi(s) + j * (C::BK * kRowBytes), &tma_a, tm * kBM + j * C::EPR, k0, p.a_once);
-          }
+          return wait_counter(src.counters() + (l - 1), (int)gridDim.x, err);
+        };
+        bool open = !src.a_stable();
+        if (open && !gate()) {
+          ok = false;
+          break;
+        }
+        // B loads held back until the gate opens: (stage, k0, tn, b)
+        int32_t pend[C::STAGES][4];
+        int npend = 0;
+        auto load = [&](int st, void* dst, const CUtensorMap* map, int32_t c0, int32_t c1, int32_t b, bool hint) {
+          if (hint) lcd::tma_load_3d_hint(dst, map, &full[st], c0, c1, b, once);
+          else if (EPI == 2) lcd::tma_load_3d_hint(dst, map, &full[st], c0, c1, b, keep);
+          else lcd::tma_load_3d(dst, map, &full[st], c0, c1, b);
+        };
+        auto load_b = [&](int st, int32_t k0, int32_t tn, int32_t b) {
           if (!p.b_mn) {
-            load(b_hi(s), &tma_b, k0, tn * BN, p.b_once);
+            load(st, b_hi(st), tb, k0, tn * BN, b, p.b_once);
           } else {
 #pragma unroll
             for (int j = 0; j < BN / C::EPR; j++)
-              load(b_hi(s) + j * (C::BK * kRowBytes), &tma_b, tn * BN + j * C::EPR, k0, p.b_once);
+              load(st, b_hi(st) + j * (C::BK * kRowBytes), tb, tn * BN + j * C::EPR, k0, b, p.b_once);
           }
-          filled |= 1u << s;
-          last_par = (last_par & ~(1u << s)) | (ph << s);
-          if (++s == C::STAGES) {
-            s = 0;
-            ph ^= 1u;
+        };
+        auto release = [&]() -> bool {
+          if (!gate()) return false;
+          for (int i = 0; i < npend; i++) load_b(pend[i][0], pend[i][1], pend[i][2], pend[i][3]);
+          npend = 0;
+          open = true;
+          return true;
+        };
+        for (int32_t u = blockIdx.x; ok && u < p.units; u += gridDim.x) {
+          int32_t b, split, tm, tn;
+          unit_coords(p, u, &b, &split, &tm, &tn);
+          const int32_t kb = split * p.kt_per_split;
+          const int32_t ke = min(kb + p.kt_per_split, p.k_tiles);
+          for (int32_t kt = kb; kt < ke; kt++) {
+            // every slot holds an A tile waiting for its B: open the gate before reusing one
+            if (!open && npend == C::STAGES && !release()) {
+              ok = false;
+              break;
+            }
+            if (!lcd::mbar_wait(&empty[s], ph ^ 1u, err)) {
+              ok = false;
+              break;
+            }
+            lcd::mbar_arrive_expect_tx(&full[s], kStageTx);
+            const int32_t k0 = kt * C::BK;
+            if (!p.a_mn) {
+              load(s, a_hi(s), ta, k0, tm * kBM, b, p.a_once);
+            } else {
+#pragma unroll
+              for (int j = 0; j < kBM / C::EPR; j++)
+                load(s, a_hi(s) + j * (C::BK * kRowBytes), ta, tm * kBM + j * C::EPR, k0, b, p.a_once);
+            }
+            if (open) {
+              load_b(s, k0, tn, b);
+            } else {
+              pend[npend][0] = s;
+              pend[npend][1] = k0;
+              pend[npend][2] = tn;
+              pend[npend][3] = b;
+              npend++;
+            }
+            filled |= 1u << s;
+            last_par = (last_par & ~(1u << s)) | (ph << s);
+            if (++s == C::STAGES) {
+              s = 0;
+              ph ^= 1u;
+            }
           }
         }
+        // a product with fewer k-tiles than stages (or none for this CTA) still opens its gate
+        if (ok && !open && !release()) ok = false;
       }
       // never leave a bulk copy in flight into shared memory that is about to be released
       for (int t = 0; t < C::STAGES; t++)
-        if (filled & (1u << t)) lcd::mbar_wait(&full[t], (last_par >> t) & 1u, p.err);
+        if (filled & (1u << t)) lcd::mbar_wait(&full[t], (last_par >> t) & 1u, err);
     }
   } else if (warp == 1) {
     if (lane == 0) {
@@ -548,6 +763,8 @@ __global__ void __launch_bounds__(Cfg<BN, TF32X3, PAIR>::THREADS, 1)
       uint32_t ph = 0;
       int32_t h = 0;  // hand-offs so far
       bool ok = true;
+      for (int l = 0; ok && l < src.layers(); l++) {
+      decltype(auto) p = src.kp(l);  // a chain's are copied to registers once per product
       for (int32_t u = blockIdx.x; ok && u < p.units; u += gridDim.x) {
         int32_t b, split, tm, tn;
         unit_coords(p, u, &b, &split, &tm, &tn);
@@ -559,14 +776,14 @@ __global__ void __launch_bounds__(Cfg<BN, TF32X3, PAIR>::THREADS, 1)
         for (int32_t c0 = kb; ok && c0 < ke; c0 += C::KC, h++) {
         const int32_t c1 = min(c0 + C::KC, ke);
         const int acc = h & 1;
-        if (!lcd::mbar_wait(&tempty[acc], ((h >> 1) & 1) ^ 1u, p.err)) {
+        if (!lcd::mbar_wait(&tempty[acc], ((h >> 1) & 1) ^ 1u, err)) {
           ok = false;
           break;
         }
         lcd::tc_fence_after();
         const uint32_t d_tmem = tmem_base + acc * BN;
         for (int32_t kt = c0; kt < c1; kt++) {
-          if (!lcd::mbar_wait(TF32X3 ? &conv[s] : &full[s], ph, p.err)) {
+          if (!lcd::mbar_wait(TF32X3 ? &conv[s] : &full[s], ph, err)) {
             ok = false;
             break;
           }
@@ -612,33 +829,49 @@ __global__ void __launch_bounds__(Cfg<BN, TF32X3, PAIR>::THREADS, 1)
         lcd::umma_commit(&tfull[acc]);
         }
       }
+      }
       // every MMA this thread issued has retired before TMEM is released
       lcd::umma_commit(drain);
-      lcd::mbar_wait(drain, 0, p.err);
+      lcd::mbar_wait(drain, 0, err);
     }
   } else if (warp < 6) {
     // ---------------- epilogue ----------------
     // Warp q owns TMEM lanes (tile rows) 32q..32q+31; lane l holds tile row 32q + l.
     const int q = warp & 3;
     const uint32_t lane_base = tmem_base + ((uint32_t)(q * 32) << 16);
-    const bool split_mode = p.splits > 1 && !PAIR;
     int32_t h = 0;
     bool ok = true;
     lcd::griddep_wait();
+    for (int l = 0; ok && l < src.layers(); l++) {
+    decltype(auto) p = src.kp(l);  // a chain's are copied to registers once per product
+    const bool split_mode = p.splits > 1 && !PAIR;
     for (int32_t u = blockIdx.x; ok && u < p.units; u += gridDim.x) {
       int32_t b, split, tm, tn;
       unit_coords(p, u, &b, &split, &tm, &tn);
       const int32_t m = tm * kBM + q * 32 + lane;
       const int64_t c_row = p.c_off + (int64_t)b * p.c_bs + (int64_t)m * p.c_ms;
       // one 32-column group [n0, n0 + 32) of this lane's row, straight from the tcgen05.ld registers
+      // (warp-uniform branches: n0, cnt and the block's row count are the same for all lanes)
       auto emit = [&](const uint32_t (&r)[32], int32_t n0) {
         const int32_t cnt = min(32, p.N - n0);
-        if (m >= p.M || cnt <= 0) return;
+        const int32_t m0w = tm * kBM + q * 32;
+        const int32_t rows = min(32, p.M - m0w);
+        if (cnt <= 0 || rows <= 0) return;
         float v[32];
 #pragma unroll
         for (int j = 0; j < 32; j++) v[j] = __uint_as_float(r[j]);
-        if (split_mode) store_partial(p, v, partial_row(p, split, b, m) + n0, cnt);
-        else store_row<EPI>(p, v, c_row + (int64_t)n0 * p.c_ns, cnt);
+        float* stage = epi_stage + (warp - 2) * (32 * 36);
+        if (split_mode) {
+          if (!PAIR && cnt == 32 && (p.N % 4) == 0)
+            store_tile32<EPI, true>(p, v, stage, 0, partial_row(p, split, b, m0w) + n0, p.N, rows);
+          else if (m < p.M)
+            store_partial(p, v, partial_row(p, split, b, m) + n0, cnt);
+        } else if (!PAIR && p.vec && cnt == 32) {
+          store_tile32<EPI, false>(p, v, stage, p.c_off + (int64_t)b * p.c_bs + (int64_t)m0w * p.c_ms + n0, nullptr,
+                                   0, rows);
+        } else if (m < p.M) {
+          store_row<EPI>(p, v, c_row + (int64_t)n0 * p.c_ns, cnt);
+        }
       };
       if constexpr (TF32X3) {
         // Running sum of the chunk accumulators, kept in a third TMEM region (columns 2*BN..3*BN)
@@ -692,13 +925,19 @@ __global__ void __launch_bounds__(Cfg<BN, TF32X3, PAIR>::THREADS, 1)
         constexpr int HB = BN / 2;   // floats per receive-buffer row
         constexpr int GH = BN / 64;  // 32-column groups per half
         const int acc = h & 1;
-        if (!lcd::mbar_wait(&tfull[acc], (h >> 1) & 1, p.err)) break;
+        if (!lcd::mbar_wait(&tfull[acc], (h >> 1) & 1, p.err)) {
+          ok = false;
+          break;
+        }
         lcd::tc_fence_after();
         const int row = q * 32 + lane;
         const uint32_t sw = (uint32_t)(row & 7);
         const uint32_t peer = rank ^ 1u;
         // (1) the peer's half, once the peer has consumed what this CTA sent for the last tile
-        if (!lcd::mbar_wait_cluster(recv_free, (h & 1) ^ 1, p.err)) break;
+        if (!lcd::mbar_wait_cluster(recv_free, (h & 1) ^ 1, p.err)) {
+          ok = false;
+          break;
+        }
         {
           const uint32_t dst = lcd::mapa_shared(lcd::smem_u32(recv + row * HB), peer);
           uint32_t r[GH][32];
@@ -718,7 +957,10 @@ __global__ void __launch_bounds__(Cfg<BN, TF32X3, PAIR>::THREADS, 1)
         }
         lcd::mbar_arrive_remote(lcd::mapa_shared(lcd::smem_u32(recv_full), peer));
         // (2) this CTA's half: its own accumulator plus the peer's, then the epilogue
-        if (!lcd::mbar_wait_cluster(recv_full, h & 1, p.err)) break;
+        if (!lcd::mbar_wait_cluster(recv_full, h & 1, p.err)) {
+          ok = false;
+          break;
+        }
         const float* src = recv + row * HB;
 #pragma unroll 1
         for (int gl = 0; gl < GH; gl++) {
@@ -762,8 +1004,26 @@ __global__ void __launch_bounds__(Cfg<BN, TF32X3, PAIR>::THREADS, 1)
         h++;
       } else {
         const int acc = h & 1;
-        if (!lcd::mbar_wait(&tfull[acc], (h >> 1) & 1, p.err)) break;
+        if (!lcd::mbar_wait(&tfull[acc], (h >> 1) & 1, p.err)) {
+          ok = false;
+          break;
+        }
         lcd::tc_fence_after();
+        // The epilogue's reads (master weights, mask, old C) wait on HBM group after group; pull
+        // the next unit's rows into L2 now, a tile ahead, so that they come from L2 then.
+        if (!split_mode && p.vec && (EPI != 0 || p.beta != 0.0f) && u + (int32_t)gridDim.x < p.units) {
+          int32_t b2, s2, tm2, tn2;
+          unit_coords(p, u + (int32_t)gridDim.x, &b2, &s2, &tm2, &tn2);
+          const int32_t m2 = tm2 * kBM + q * 32 + lane;
+          const int32_t n2 = tn2 * BN;
+          if (m2 < p.M && n2 < p.N) {
+            const int es = (EPI == 2 || p.c_dtype == LC_F32) ? 4 : 2;
+            const char* src = static_cast<const char*>(EPI == 0 ? static_cast<const void*>(p.c) : p.aux) +
+                              (p.c_off + (int64_t)b2 * p.c_bs + (int64_t)m2 * p.c_ms + n2) * es;
+            const int32_t bytes = min(BN, p.N - n2) * es;
+            for (int32_t off = 0; off < bytes; off += 128) asm volatile("prefetch.global.L2 [%0];" ::"l"(src + off));
+          }
+        }
 #pragma unroll 1
         for (int g = 0; g < BN / 32; g++) {
           uint32_t r[32];
@@ -804,12 +1064,25 @@ __global__ void __launch_bounds__(Cfg<BN, TF32X3, PAIR>::THREADS, 1)
         }
       }
     }
+    // chain: this warp's part of product l is stored.  The four epilogue warps count themselves
+    // in shared memory (they reach product l + 1 only after every CTA finished product l, so the
+    // count goes up in whole groups of four) and the last of each group publishes the CTA to the
+    // producers of product l + 1.
+    if (src.counters() != nullptr) {
+      __threadfence();
+      __syncwarp();
+      if (lane == 0 && (atomicAdd(layer_done, 1u) & 3u) == 3u)
+        asm volatile("red.release.gpu.global.add.s32 [%0], 1;" ::"l"(src.counters() + l) : "memory");
+    }
+    }
   } else if constexpr (TF32X3) {
     // ---------------- 3xTF32 split ----------------
     const int ct = threadIdx.x - 192;  // 0..127
     int s = 0;
     uint32_t ph = 0;
     bool ok = true;
+    for (int l = 0; ok && l < src.layers(); l++) {
+    decltype(auto) p = src.kp(l);  // a chain's are copied to registers once per product
     for (int32_t u = blockIdx.x; ok && u < p.units; u += gridDim.x) {
       int32_t b, split, tm, tn;
       unit_coords(p, u, &b, &split, &tm, &tn);
@@ -854,6 +1127,7 @@ __global__ void __launch_bounds__(Cfg<BN, TF32X3, PAIR>::THREADS, 1)
         }
       }
     }
+    }
   }
 
   __syncthreads();
@@ -863,6 +1137,21 @@ __global__ void __launch_bounds__(Cfg<BN, TF32X3, PAIR>::THREADS, 1)
   }
   // neither CTA of a pair leaves while the other may still access its shared memory
   if constexpr (PAIR) lcd::cluster_sync();
+}
+
+template <int BN, bool TF32X3, int EPI, bool PAIR>
+__global__ void __launch_bounds__(Cfg<BN, TF32X3, PAIR>::THREADS, 1)
+    gemm_tc_kernel(const __grid_constant__ CUtensorMap tma_a, const __grid_constant__ CUtensorMap tma_b,
+                   const __grid_constant__ KParams p) {
+  gemm_body<BN, TF32X3, EPI, PAIR>(OneProduct{&tma_a, &tma_b, &p});
+}
+
+// A chain of skinny products (BN = 64, 16-bit inputs, CTA pairs): the pipeline's layer loop of
+// one microbatch in one cooperative launch.
+template <int EPI>
+__global__ void __launch_bounds__(Cfg<64, false, true>::THREADS, 1)
+    gemm_chain_kernel(const __grid_constant__ ChainParams cp) {
+  gemm_body<64, false, EPI, true>(ChainSrc{&cp});
 }
 
 // ---- split-K reduce for many splits: C = epilogue(sum_s partial[s]), splits summed in order -----
@@ -1112,7 +1401,22 @@ bool tma_operand_ok(const GemmOperand& o, int in_dtype) {
   return true;
 }
 
-lc_status gemm_run(lc_context* ctx, cudaStream_t s, const GemmProblem& pr, lc_contract_plan* plan, bool dry_run) {
+}  // namespace lc
+
+namespace {
+
+// Everything a launch of one product needs, decided once: orientation, tile width, split,
+// CTA pairs, tensor maps and the kernel parameters.
+struct Planned {
+  KParams p{};
+  CUtensorMap ta, tb;
+  int bn = 64;
+  bool tf32x3 = false, pair = false;
+  int64_t pair_clusters = 0, tiles = 0, units = 0, splits = 1, M = 0, N = 0;
+};
+
+lc_status plan_gemm(lc_context* ctx, const lc::GemmProblem& pr, lc_contract_plan* plan, bool dry_run, Planned* out) {
+  using namespace lc;
   GemmOperand A = pr.a, B = pr.b;
   uint64_t M = pr.m, N = pr.n;
   int64_t c_ms = pr.c_m_stride, c_ns = pr.c_n_stride;
@@ -1196,7 +1500,8 @@ lc_status gemm_run(lc_context* ctx, cudaStream_t s, const GemmProblem& pr, lc_co
   }
   if (dry_run) return LC_OK;
 
-  CUtensorMap ta, tb;
+  CUtensorMap& ta = out->ta;
+  CUtensorMap& tb = out->tb;
   lc_status st;
   const void* abase = static_cast<const uint8_t*>(A.data) + A.offset * es;
   const void* bbase = static_cast<const uint8_t*>(B.data) + B.offset * es;
@@ -1220,7 +1525,8 @@ lc_status gemm_run(lc_context* ctx, cudaStream_t s, const GemmProblem& pr, lc_co
   }
   if (st) return st;
 
-  KParams p{};
+  KParams& p = out->p;
+  p = KParams{};
   p.M = (int32_t)M;
   p.N = (int32_t)N;
   p.k_tiles = (int32_t)k_tiles;
@@ -1266,6 +1572,33 @@ lc_status gemm_run(lc_context* ctx, cudaStream_t s, const GemmProblem& pr, lc_co
   p.aux = pr.aux;
   p.aux2 = pr.aux2;
   p.lr = pr.lr;
+  out->bn = bn;
+  out->tf32x3 = tf32x3;
+  out->pair = pair;
+  out->pair_clusters = pair_clusters;
+  out->tiles = tiles;
+  out->units = units;
+  out->splits = splits;
+  out->M = (int64_t)M;
+  out->N = (int64_t)N;
+  return LC_OK;
+}
+
+}  // namespace
+
+namespace lc {
+
+lc_status gemm_run(lc_context* ctx, cudaStream_t s, const GemmProblem& pr, lc_contract_plan* plan, bool dry_run) {
+  Planned pl;
+  lc_status st = plan_gemm(ctx, pr, plan, dry_run, &pl);
+  if (st || dry_run) return st;
+  KParams& p = pl.p;
+  const CUtensorMap& ta = pl.ta;
+  const CUtensorMap& tb = pl.tb;
+  const int bn = pl.bn;
+  const bool tf32x3 = pl.tf32x3, pair = pl.pair;
+  const int64_t pair_clusters = pl.pair_clusters, tiles = pl.tiles, units = pl.units, splits = pl.splits;
+  const uint64_t M = (uint64_t)pl.M, N = (uint64_t)pl.N;
   // Split-K scratch: the partial tiles and, for the in-kernel fixup (up to kFixupMaxSplits splits,
   // where each reducing warp sums few partials), one arrival counter per (batch, tile, epilogue
   // warp).  On the context's own stream the context keeps both between calls (its counters are
@@ -1362,6 +1695,89 @@ lc_status gemm_run(lc_context* ctx, cudaStream_t s, const GemmProblem& pr, lc_co
   }
   if (scratch) scratch_free(scratch, s);
   return st;
+}
+
+lc_status gemm_chain_run(lc_context* ctx, cudaStream_t s, const GemmProblem* probs, int n, bool a_stable,
+                         int max_clusters, bool* chained) {
+  *chained = false;
+  static const bool env_off = [] {
+    const char* e = getenv("LC_GEMM_CHAIN");  // "0": run chains as separate launches
+    return e != nullptr && e[0] == '0';
+  }();
+  if (env_off || n <= 0 || n > kMaxChain) return LC_OK;
+  const int epi = probs[0].epi;
+  if (epi != 0 && epi != 1) return LC_OK;
+  thread_local std::unique_ptr<ChainParams> cp_holder;
+  if (!cp_holder) cp_holder.reset(new ChainParams());
+  ChainParams& cp = *cp_holder;
+  int64_t clusters = 0;
+  for (int i = 0; i < n; i++) {
+    if (probs[i].epi != epi) return LC_OK;
+    Planned pl;
+    lc_status st = plan_gemm(ctx, probs[i], nullptr, false, &pl);
+    if (st) return st;
+    if (!pl.pair || pl.bn != 64) return LC_OK;
+    cp.p[i] = pl.p;
+    cp.a[i] = pl.ta;
+    cp.b[i] = pl.tb;
+    clusters = std::max<int64_t>(clusters, pl.pair_clusters);
+  }
+  if (max_clusters > 0 && clusters > max_clusters) {
+    // as few waves as the cap allows, spread evenly over the pairs
+    const int64_t waves = ceil_div(clusters, max_clusters);
+    clusters = ceil_div(clusters, waves);
+  }
+  cp.n = n;
+  cp.a_stable = a_stable ? 1 : 0;
+  // counters per stream slot: chains on different streams may run at the same time
+  int slot = -1;
+  for (int i = 0; i < kChainStreams; i++)
+    if (ctx->chain_stream[i] == s || ctx->chain_stream[i] == nullptr) {
+      slot = i;
+      break;
+    }
+  if (slot < 0) return LC_OK;  // more concurrent chain streams than slots: run the products one by one
+  if (ctx->chain_cnt == nullptr) {
+    cudaError_t e = cudaMalloc(&ctx->chain_cnt, kChainStreams * kMaxChain * sizeof(int));
+    if (e != cudaSuccess) return cuda_fail(e, "chain counters");
+  }
+  ctx->chain_stream[slot] = s;
+  int* counters = ctx->chain_cnt + slot * kMaxChain;
+  cp.counters = counters;
+  cudaError_t e = cudaMemsetAsync(counters, 0, (size_t)n * sizeof(int), s);
+  if (e != cudaSuccess) return cuda_fail(e, "chain counters");
+  auto kern = epi == 0 ? gemm_chain_kernel<0> : gemm_chain_kernel<1>;
+  using C = Cfg<64, false, true>;
+  static bool attr_set[2][64] = {};
+  if (!attr_set[epi][ctx->device % 64]) {
+    e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM);
+    if (e != cudaSuccess) return cuda_fail(e, "cudaFuncSetAttribute(gemm chain)");
+    attr_set[epi][ctx->device % 64] = true;
+  }
+  cudaLaunchConfig_t cfg{};
+  cfg.gridDim = dim3((unsigned)(2 * clusters));
+  cfg.blockDim = dim3(C::THREADS);
+  cfg.dynamicSmemBytes = C::SMEM;
+  cfg.stream = s;
+  cudaLaunchAttribute at[2];
+  // every CTA of the chain waits on every other between products: all must be resident at once
+  at[0].id = cudaLaunchAttributeCooperative;
+  at[0].val.cooperative = 1;
+  at[1].id = cudaLaunchAttributeClusterDimension;
+  at[1].val.clusterDim.x = 2;
+  at[1].val.clusterDim.y = 1;
+  at[1].val.clusterDim.z = 1;
+  cfg.attrs = at;
+  cfg.numAttrs = 2;
+  e = cudaLaunchKernelEx(&cfg, kern, cp);
+  if (e != cudaSuccess) {
+    // e.g. more clusters than can be co-resident: leave the chain to one-by-one launches
+    cudaGetLastError();
+    return LC_OK;
+  }
+  record_launch(ctx, epi == 0 ? "gemm_bf16_chain_n64" : "gemm_bf16_chain_mask_n64");
+  *chained = true;
+  return LC_OK;
 }
 
 lc_status gemm_fill(lc_context* ctx, cudaStream_t s, const GemmProblem& pr) {

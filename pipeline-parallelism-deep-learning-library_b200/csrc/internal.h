@@ -24,7 +24,13 @@ struct lc_context {
   size_t split_part_bytes = 0;
   int* split_cnt = nullptr;
   size_t split_cnt_n = 0;
+  // Per-product completion counters of GEMM chain launches (zeroed before each chain), one
+  // block of counters per stream that launches chains.
+  int* chain_cnt = nullptr;
+  void* chain_stream[4] = {nullptr, nullptr, nullptr, nullptr};
 };
+
+constexpr int kChainStreams = 4;
 
 namespace lc {
 

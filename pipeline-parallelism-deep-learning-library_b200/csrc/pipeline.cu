@@ -195,6 +195,12 @@ struct lc_pipeline {
   bool train_mode = false;
   lc_context* ctx = nullptr;
   cudaStream_t s_fwd = nullptr, s_bwd = nullptr;
+  // Training mode: extra compute streams.  In 1F1B the forwards of different microbatches are
+  // independent, so are the backwards, and B(m) needs only F(m): forwards run on the even
+  // streams (0 = the context stream), backwards on the odd ones, microbatch m on pair m % (K/2),
+  // so K/2 forwards and K/2 backwards can share the GPU and hide each other's per-layer gaps.
+  std::vector<cudaStream_t> s_work;  // streams 1 .. K-1 (K = kernels that may share the GPU)
+  int n_streams = 1;
   ncclComm_t comm_fwd = nullptr, comm_bwd = nullptr;
   uint64_t first = 0, count = 0, B = 0;
   std::vector<float*> master, dw, pre;
@@ -208,7 +214,10 @@ struct lc_pipeline {
   float* loss_dev = nullptr;
   float* loss_host = nullptr;  // pinned
   cudaEvent_t ev_start = nullptr, ev_end = nullptr, ev_fwd_join = nullptr, ev_bwd_join = nullptr;
+  cudaEvent_t ev_inputs = nullptr;          // the step's inputs are on the device
+  std::vector<cudaEvent_t> ev_work_join;     // per extra compute stream: its last op of the step
   std::vector<cudaEvent_t> ev_fr, ev_fd, ev_br, ev_bd;
+  std::vector<cudaEvent_t> ev_fdone;  // microbatch m's forward (and loss gradient) complete
   float last_ms = 0.0f;
   bool aborted = false;
 
@@ -217,6 +226,11 @@ struct lc_pipeline {
   bool is_first() const { return rank == 0; }
   bool is_last() const { return rank + 1 == world; }
   cudaStream_t comp() const { return ctx->stream; }
+  cudaStream_t work(int i) const { return i == 0 ? ctx->stream : s_work[i - 1]; }
+  cudaStream_t fwd_stream(uint64_t m) const { return n_streams > 1 ? work((int)(2 * (m % (n_streams / 2)))) : ctx->stream; }
+  cudaStream_t back_stream(uint64_t m) const {
+    return n_streams > 1 ? work((int)(2 * (m % (n_streams / 2)) + 1)) : ctx->stream;
+  }
   size_t es() const { return train_mode ? 2 : 4; }
 };
 
@@ -246,7 +260,19 @@ lc_status setup(lc_pipeline* p) {
   CU(cudaEventCreate(&p->ev_end));
   CU(cudaEventCreateWithFlags(&p->ev_fwd_join, cudaEventDisableTiming));
   CU(cudaEventCreateWithFlags(&p->ev_bwd_join, cudaEventDisableTiming));
-  for (auto* v : {&p->ev_fr, &p->ev_fd, &p->ev_br, &p->ev_bd}) {
+  CU(cudaEventCreateWithFlags(&p->ev_inputs, cudaEventDisableTiming));
+  if (p->train_mode) {
+    static const int env_streams = [] {
+      const char* e = getenv("LC_PIPE_STREAMS");  // tuning override: compute streams (1, 2 or 4)
+      return e ? atoi(e) : 0;
+    }();
+    p->n_streams = env_streams == 1 || env_streams == 2 || env_streams == 4 ? env_streams : 4;
+    p->s_work.resize(p->n_streams - 1);
+    p->ev_work_join.resize(p->n_streams - 1);
+    for (auto& q : p->s_work) CU(cudaStreamCreateWithFlags(&q, cudaStreamNonBlocking));
+    for (auto& e : p->ev_work_join) CU(cudaEventCreateWithFlags(&e, cudaEventDisableTiming));
+  }
+  for (auto* v : {&p->ev_fr, &p->ev_fd, &p->ev_br, &p->ev_bd, &p->ev_fdone}) {
     v->resize(mbs);
     for (auto& e : *v) CU(cudaEventCreateWithFlags(&e, cudaEventDisableTiming));
   }
@@ -325,7 +351,7 @@ GemmProblem bf16_problem(uint64_t m, uint64_t n, uint64_t k) {
 }
 
 // H[l+1][rows] = relu(H[l][rows] @ Wb_l)
-lc_status fwd_layer(lc_pipeline* p, uint64_t l, uint64_t row0, uint64_t rows) {
+GemmProblem fwd_problem(lc_pipeline* p, uint64_t l, uint64_t row0, uint64_t rows) {
   const uint64_t k = p->win(l), n = p->wout(l);
   GemmProblem g = bf16_problem(rows, n, k);
   g.a.data = p->H[l];
@@ -344,11 +370,11 @@ lc_status fwd_layer(lc_pipeline* p, uint64_t l, uint64_t row0, uint64_t rows) {
   g.c_m_stride = (int64_t)n;
   g.c_n_stride = 1;
   g.relu = 1;
-  return gemm_run(p->ctx, p->comp(), g, nullptr, false);
+  return g;
 }
 
 // out[rows] = (dP[l][rows] @ Wb_l^T) where H[l][rows] > 0
-lc_status dgrad_layer(lc_pipeline* p, uint64_t l, uint64_t row0, uint64_t rows, void* out) {
+GemmProblem dgrad_problem(lc_pipeline* p, uint64_t l, uint64_t row0, uint64_t rows, void* out) {
   const uint64_t k = p->wout(l), n = p->win(l);
   GemmProblem g = bf16_problem(rows, n, k);
   g.a.data = p->dP[l];
@@ -368,7 +394,22 @@ lc_status dgrad_layer(lc_pipeline* p, uint64_t l, uint64_t row0, uint64_t rows, 
   g.c_n_stride = 1;
   g.epi = 1;
   g.aux = p->H[l];  // the layer's input, same [B, n] layout as the output
-  return gemm_run(p->ctx, p->comp(), g, nullptr, false);
+  return g;
+}
+
+// The stage's layer loop of one microbatch as one chain launch when the products allow it
+// (the weights are read-only between the steps' weight updates), else one launch per layer.
+lc_status run_products(lc_pipeline* p, cudaStream_t s, const std::vector<GemmProblem>& probs) {
+  if (probs.empty()) return LC_OK;
+  bool chained = false;
+  // with K compute streams, K chains share the GPU: each takes 1/K of the SMs' CTA pairs
+  // (16 of 64 at width 8192 and K = 4, four tiles per pair)
+  const int cap = p->n_streams > 1 ? (int)std::max<int64_t>(1, (p->ctx->sm_count - 4) / (2 * p->n_streams)) : 0;
+  lc_status st = gemm_chain_run(p->ctx, s, probs.data(), (int)probs.size(), true, cap, &chained);
+  if (st || chained) return st;
+  for (const GemmProblem& g : probs)
+    if ((st = gemm_run(p->ctx, s, g, nullptr, false))) return st;
+  return LC_OK;
 }
 
 // W_l -= lr * H[l]^T @ dP[l] (K = B), Wb_l = bf16(W_l); or dW_l = H[l]^T @ dP[l] when lr == 0
@@ -573,10 +614,13 @@ lc_status lc_pipeline_destroy(lc_pipeline* p) {
   for (void* q : {p->gsend, p->dbuf, p->dbuf2, (void*)p->x_dev, (void*)p->t_dev, (void*)p->part, (void*)p->loss_dev})
     if (q) cudaFree(q);
   if (p->loss_host) cudaFreeHost(p->loss_host);
-  for (auto* v : {&p->ev_fr, &p->ev_fd, &p->ev_br, &p->ev_bd})
+  for (auto* v : {&p->ev_fr, &p->ev_fd, &p->ev_br, &p->ev_bd, &p->ev_fdone})
     for (auto e : *v) cudaEventDestroy(e);
-  for (auto e : {p->ev_start, p->ev_end, p->ev_fwd_join, p->ev_bwd_join})
+  for (auto e : {p->ev_start, p->ev_end, p->ev_fwd_join, p->ev_bwd_join, p->ev_inputs})
     if (e) cudaEventDestroy(e);
+  for (auto e : p->ev_work_join) cudaEventDestroy(e);
+  for (auto q : p->s_work)
+    if (q) cudaStreamDestroy(q);
   if (p->s_fwd) cudaStreamDestroy(p->s_fwd);
   if (p->s_bwd) cudaStreamDestroy(p->s_bwd);
   if (p->ctx) lc_context_destroy(p->ctx);
@@ -681,6 +725,8 @@ lc_status lc_pipeline_step(lc_pipeline* p, const float* x, const float* target_o
   const cudaMemcpyKind kind = inputs_on_device ? cudaMemcpyDeviceToDevice : cudaMemcpyHostToDevice;
   if (p->is_first()) CU(cudaMemcpyAsync(p->x_dev, x, p->B * p->widths[0] * 4, kind, cs));
   if (p->is_last()) CU(cudaMemcpyAsync(p->t_dev, target_or_dy, p->B * p->widths.back() * 4, kind, cs));
+  CU(cudaEventRecord(p->ev_inputs, cs));
+  for (cudaStream_t q : p->s_work) CU(cudaStreamWaitEvent(q, p->ev_inputs, 0));
   const float n_total = (float)(p->B * p->widths.back());
 
   for (uint64_t i = 0; i < n_ops && !st; i++) {
@@ -688,50 +734,63 @@ lc_status lc_pipeline_step(lc_pipeline* p, const float* x, const float* target_o
     const uint64_t m = (uint64_t)(fwd ? order[i] : -order[i]) - 1;
     const uint64_t row0 = m * mb;
     if (fwd) {
+      const cudaStream_t fs = p->fwd_stream(m);
       void* in = (uint8_t*)p->H[0] + row0 * w0 * es;
       if (p->is_first()) {
         if (p->train_mode) {
-          to_bf16_kernel<<<blocks_for(p->ctx, mb * w0), 256, 0, cs>>>(p->x_dev + row0 * w0, (uint16_t*)in, mb * w0);
+          to_bf16_kernel<<<blocks_for(p->ctx, mb * w0), 256, 0, fs>>>(p->x_dev + row0 * w0, (uint16_t*)in, mb * w0);
           record_launch(p->ctx, "pipeline_input_to_bf16");
         } else {
-          CU(cudaMemcpyAsync(in, p->x_dev + row0 * w0, mb * w0 * 4, cudaMemcpyDeviceToDevice, cs));
+          CU(cudaMemcpyAsync(in, p->x_dev + row0 * w0, mb * w0 * 4, cudaMemcpyDeviceToDevice, fs));
         }
       } else {
         NC(nccl().Recv(in, mb * w0, nt, p->rank - 1, p->comm_fwd, p->s_fwd));
         CU(cudaEventRecord(p->ev_fr[m], p->s_fwd));
-        CU(cudaStreamWaitEvent(cs, p->ev_fr[m], 0));
+        CU(cudaStreamWaitEvent(fs, p->ev_fr[m], 0));
       }
-      for (uint64_t l = 0; l < p->count && !st; l++)
-        st = p->train_mode ? fwd_layer(p, l, row0, mb) : ref_forward(p, l, row0, mb);
+      if (p->train_mode) {
+        std::vector<GemmProblem> probs;
+        for (uint64_t l = 0; l < p->count; l++) probs.push_back(fwd_problem(p, l, row0, mb));
+        st = run_products(p, fs, probs);
+      } else {
+        for (uint64_t l = 0; l < p->count && !st; l++) st = ref_forward(p, l, row0, mb);
+      }
       if (st) break;
       void* outp = (uint8_t*)p->H[p->count] + row0 * wl * es;
       if (!p->is_last()) {
-        CU(cudaEventRecord(p->ev_fd[m], cs));
+        CU(cudaEventRecord(p->ev_fd[m], fs));
         CU(cudaStreamWaitEvent(p->s_fwd, p->ev_fd[m], 0));
         NC(nccl().Send(outp, mb * wl, nt, p->rank + 1, p->comm_fwd, p->s_fwd));
       } else if (p->train_mode) {
-        mse_relu_kernel<<<kMseBlocks, kMseThreads, 0, cs>>>((const uint16_t*)outp, p->t_dev + row0 * wl,
+        mse_relu_kernel<<<kMseBlocks, kMseThreads, 0, fs>>>((const uint16_t*)outp, p->t_dev + row0 * wl,
                                                           (uint16_t*)p->dP[p->count - 1] + row0 * wl, mb * wl, n_total,
                                                           p->part + m * kMseBlocks);
         record_launch(p->ctx, "pipeline_mse_relu");
       }
+      CU(cudaEventRecord(p->ev_fdone[m], fs));
     } else {
+      // backward of microbatch m on its own stream, after its forward (activations, masks, the
+      // loss gradient) is complete
+      const cudaStream_t bs = p->back_stream(m);
+      CU(cudaStreamWaitEvent(bs, p->ev_fdone[m], 0));
       // incoming gradient for the stage's last layer
       const float* g_ref = nullptr;
       if (!p->is_last()) {
         void* gin = (uint8_t*)p->dP[p->train_mode ? p->count - 1 : 0] + row0 * wl * es;
         NC(nccl().Recv(gin, mb * wl, nt, p->rank + 1, p->comm_bwd, p->s_bwd));
         CU(cudaEventRecord(p->ev_br[m], p->s_bwd));
-        CU(cudaStreamWaitEvent(cs, p->ev_br[m], 0));
+        CU(cudaStreamWaitEvent(bs, p->ev_br[m], 0));
         g_ref = (const float*)gin;
       } else {
         g_ref = p->t_dev + row0 * wl;  // reference mode: dy
       }
       if (p->train_mode) {
-        for (uint64_t l = p->count; l-- > 0 && !st;) {
-          if (l > 0) st = dgrad_layer(p, l, row0, mb, p->dP[l - 1]);
-          else if (!p->is_first()) st = dgrad_layer(p, 0, row0, mb, p->gsend);
+        std::vector<GemmProblem> probs;
+        for (uint64_t l = p->count; l-- > 0;) {
+          if (l > 0) probs.push_back(dgrad_problem(p, l, row0, mb, p->dP[l - 1]));
+          else if (!p->is_first()) probs.push_back(dgrad_problem(p, 0, row0, mb, p->gsend));
         }
+        st = run_products(p, bs, probs);
       } else {
         // g is consumed by the activation backward (into dbuf) before the dgrad GEMM writes dx,
         // so dx can land in the buffer g came from (dbuf2) without any op reading and writing
@@ -747,11 +806,16 @@ lc_status lc_pipeline_step(lc_pipeline* p, const float* x, const float* target_o
       }
       if (st) break;
       if (!p->is_first()) {
-        CU(cudaEventRecord(p->ev_bd[m], cs));
+        CU(cudaEventRecord(p->ev_bd[m], bs));
         CU(cudaStreamWaitEvent(p->s_bwd, p->ev_bd[m], 0));
         NC(nccl().Send((uint8_t*)p->gsend + row0 * w0 * es, mb * w0, nt, p->rank - 1, p->comm_bwd, p->s_bwd));
       }
     }
+  }
+  // the weight updates read every microbatch's gradients: join the compute streams first
+  for (size_t i = 0; i < p->s_work.size(); i++) {
+    CU(cudaEventRecord(p->ev_work_join[i], p->s_work[i]));
+    CU(cudaStreamWaitEvent(cs, p->ev_work_join[i], 0));
   }
   if (!st && p->train_mode)
     for (uint64_t l = 0; l < p->count && !st; l++) st = wgrad_layer(p, l);

@@ -188,6 +188,13 @@ __device__ __forceinline__ uint64_t policy_evict_first() {
   return p;
 }
 
+// L2 policy for operands that many CTAs re-read while other data streams past them.
+__device__ __forceinline__ uint64_t policy_evict_last() {
+  uint64_t p;
+  asm volatile("createpolicy.fractional.L2::evict_last.b64 %0, 1.0;" : "=l"(p));
+  return p;
+}
+
 __device__ __forceinline__ void tma_load_3d_hint(void* smem_dst, const void* desc, uint64_t* bar, int32_t c0,
                                                  int32_t c1, int32_t c2, uint64_t policy) {
   asm volatile(

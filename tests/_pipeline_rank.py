@@ -1,6 +1,6 @@
-"""One rank of a multi-GPU pipeline run, started by tests/test_pipeline_multigpu.py as its own
-process (one process per GPU, as the pipeline requires).  Writes the losses and this rank's
-updated layers to an .npz file."""
+"""One rank of a pipeline run in its own process (one process per GPU, as the pipeline
+requires), started by the pipeline tests.  Writes the losses and this rank's updated layers to
+an .npz file."""
 import json
 import sys
 from pathlib import Path
@@ -16,7 +16,8 @@ from linalg_b200.pipeline import Pipeline  # noqa: E402
 
 def main():
     cfg = json.loads(sys.argv[1])
-    rank, world, uid, out = cfg["rank"], cfg["world"], bytes.fromhex(cfg["uid"]), cfg["out"]
+    rank, world, out = cfg["rank"], cfg["world"], cfg["out"]
+    uid = bytes.fromhex(cfg["uid"]) if cfg.get("uid") else None
     L, d, mb, mbs, lr, steps = cfg["layers"], cfg["width"], cfg["microbatch"], cfg["microbatches"], cfg["lr"], cfg["steps"]
     p = Pipeline(L, d, mb, mbs, lr=lr, rank=rank, world=world, device=rank, uid=uid, timeout_ms=60000)
     p.init_weights(cfg["seed"], d ** -0.5)

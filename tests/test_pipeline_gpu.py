@@ -106,3 +106,30 @@ def test_training_step_is_deterministic(gpu):
         outs.append((loss, p.get_weight(0).tobytes(), p.get_weight(1).tobytes()))
         p.close()
     assert outs[0] == outs[1]
+
+
+def test_layer_chains_equal_one_launch_per_layer(gpu, tmp_path):
+    """Each microbatch's layer loop runs as one chain launch (CTAs resident across layers);
+    the products and their order of summation are those of one launch per layer, so the
+    losses and weights match bit for bit (LC_GEMM_CHAIN=0 forces one launch per layer)."""
+    import os
+    import subprocess
+    import sys
+    here = Path(__file__).resolve().parent
+    cfg = {"layers": 6, "width": 1024, "microbatch": 64, "microbatches": 4, "lr": 1e-2, "steps": 2, "seed": 5,
+           "rank": 0, "world": 1, "uid": ""}
+    outs = {}
+    for mode in ("chain", "layers"):
+        env = dict(os.environ)
+        if mode == "layers":
+            env["LC_GEMM_CHAIN"] = "0"
+        c = dict(cfg, out=str(tmp_path / f"{mode}.npz"))
+        r = subprocess.run([sys.executable, str(here / "_pipeline_rank.py"), json.dumps(c)], env=env,
+                           capture_output=True, text=True, timeout=600)
+        assert r.returncode == 0, r.stdout + r.stderr
+        outs[mode] = np.load(tmp_path / f"{mode}.npz")
+    a, b = outs["chain"], outs["layers"]
+    assert a["losses"].tobytes() == b["losses"].tobytes()
+    assert a["losses"][1] < a["losses"][0]
+    for l in range(cfg["layers"]):
+        assert a[f"w{l}"].tobytes() == b[f"w{l}"].tobytes(), l
