@@ -27,10 +27,10 @@ struct lc_context {
   // Per-product completion counters of GEMM chain launches (zeroed before each chain), one
   // block of counters per stream that launches chains.
   int* chain_cnt = nullptr;
-  void* chain_stream[4] = {nullptr, nullptr, nullptr, nullptr};
+  void* chain_stream[8] = {};
 };
 
-constexpr int kChainStreams = 4;
+constexpr int kChainStreams = 8;
 
 namespace lc {
 

@@ -92,14 +92,40 @@ __global__ void to_bf16_kernel(const float* __restrict__ x, uint16_t* __restrict
 // MSE over the whole batch with the ReLU' of the last layer folded in:
 //   d = f32(y) - t;  part += d*d;  g = (y > 0) ? bf16((2*d)/N) : 0
 constexpr int kMseThreads = 256;
-constexpr int kMseBlocks = 64;
+constexpr int kMseBlocks = 296;  // 2 per SM: the loss gradient of one microbatch in one wave
+// dy = relu'(y) * (2 * (y - t)) / n and per-block partial sums of (y - t)^2, 8 elements at a time
+// (16-byte loads of y and g, two of t); the partials are summed in a fixed order by
+// loss_reduce_kernel, so the loss is deterministic.
 __global__ void __launch_bounds__(kMseThreads) mse_relu_kernel(const uint16_t* __restrict__ y, const float* __restrict__ t,
                                                                 uint16_t* __restrict__ g, uint64_t n, float n_total,
                                                                 float* __restrict__ part) {
   __shared__ float red[kMseThreads];
   float acc = 0.0f;
   const uint64_t stride = (uint64_t)gridDim.x * blockDim.x;
-  for (uint64_t i = blockIdx.x * (uint64_t)blockDim.x + threadIdx.x; i < n; i += stride) {
+  // 16-byte accesses only when all three arrays start 16-byte aligned (widths that are not a
+  // multiple of 8 shift microbatch rows off alignment); otherwise the element loop below does it all
+  const bool vec = ((reinterpret_cast<uintptr_t>(y) | reinterpret_cast<uintptr_t>(g) | reinterpret_cast<uintptr_t>(t)) &
+                    15u) == 0;
+  const uint64_t n8 = vec ? n / 8 : 0;
+  for (uint64_t i = blockIdx.x * (uint64_t)blockDim.x + threadIdx.x; i < n8; i += stride) {
+    const uint4 yr = __ldcs(reinterpret_cast<const uint4*>(y) + i);
+    const float4 t0 = __ldcs(reinterpret_cast<const float4*>(t) + 2 * i);
+    const float4 t1 = __ldcs(reinterpret_cast<const float4*>(t) + 2 * i + 1);
+    const uint32_t yw[4] = {yr.x, yr.y, yr.z, yr.w};
+    const float tv[8] = {t0.x, t0.y, t0.z, t0.w, t1.x, t1.y, t1.z, t1.w};
+    uint32_t gw[4];
+#pragma unroll
+    for (int e = 0; e < 8; e++) {
+      const float yv = bf16_f32((uint16_t)(e & 1 ? yw[e / 2] >> 16 : yw[e / 2] & 0xffffu));
+      const float d = __fsub_rn(yv, tv[e]);
+      acc = __fadd_rn(acc, __fmul_rn(d, d));
+      const uint32_t gb = yv > 0.0f ? bf16_bits(__fdiv_rn(__fmul_rn(2.0f, d), n_total)) : 0u;
+      if (e & 1) gw[e / 2] |= gb << 16;
+      else gw[e / 2] = gb;
+    }
+    reinterpret_cast<uint4*>(g)[i] = make_uint4(gw[0], gw[1], gw[2], gw[3]);
+  }
+  for (uint64_t i = n8 * 8 + blockIdx.x * (uint64_t)blockDim.x + threadIdx.x; i < n; i += stride) {
     const float yv = bf16_f32(y[i]);
     const float d = __fsub_rn(yv, t[i]);
     acc = __fadd_rn(acc, __fmul_rn(d, d));
@@ -263,10 +289,10 @@ lc_status setup(lc_pipeline* p) {
   CU(cudaEventCreateWithFlags(&p->ev_inputs, cudaEventDisableTiming));
   if (p->train_mode) {
     static const int env_streams = [] {
-      const char* e = getenv("LC_PIPE_STREAMS");  // tuning override: compute streams (1, 2 or 4)
+      const char* e = getenv("LC_PIPE_STREAMS");  // tuning override: compute streams (1, 2, 4 or 8)
       return e ? atoi(e) : 0;
     }();
-    p->n_streams = env_streams == 1 || env_streams == 2 || env_streams == 4 ? env_streams : 4;
+    p->n_streams = env_streams == 1 || env_streams == 2 || env_streams == 4 || env_streams == 8 ? env_streams : 4;
     p->s_work.resize(p->n_streams - 1);
     p->ev_work_join.resize(p->n_streams - 1);
     for (auto& q : p->s_work) CU(cudaStreamCreateWithFlags(&q, cudaStreamNonBlocking));
