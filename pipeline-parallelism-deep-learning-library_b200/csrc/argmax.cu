@@ -121,6 +121,11 @@ struct RowGeom {
 };
 
 __device__ __forceinline__ void row_offsets(const RowGeom& g, uint64_t r, uint64_t* xo, uint64_t* oo) {
+  if (g.rank == 1) {  // leading axes collapsed to one row stride on the host: no division
+    *xo = g.x_off + r * g.xs[0];
+    *oo = g.o_off + r * g.os[0];
+    return;
+  }
   uint64_t a = g.x_off, b = g.o_off;
   for (int d = g.rank - 1; d >= 0; d--) {
     uint64_t n = g.shape[d];
@@ -140,6 +145,46 @@ __global__ void __launch_bounds__(kThreads) argmax_rows_kernel(const float* __re
   const uint64_t rows_per_block = kThreads / lpr;
   const uint64_t row_stride = (uint64_t)gridDim.x * rows_per_block;
   const unsigned group_mask = lpr == 32 ? 0xffffffffu : (((1u << lpr) - 1u) << ((threadIdx.x & 31) / lpr * lpr));
+  if (g.vec && g.cols == 4 * (uint64_t)lpr) {
+    // one float4 per lane per row (64-float rows): load 4 rows before reducing any, so each
+    // thread keeps 4 loads in flight instead of 1
+    constexpr int R = 4;
+    for (uint64_t r0 = (uint64_t)blockIdx.x * rows_per_block * R; r0 < g.rows; r0 += row_stride * R) {
+      float4 q[R];
+      uint64_t oo[R];
+      bool act[R];
+#pragma unroll
+      for (int k = 0; k < R; k++) {
+        const uint64_t r = r0 + k * rows_per_block + threadIdx.x / lpr;
+        act[k] = r < g.rows;
+        uint64_t xo = 0;
+        oo[k] = 0;
+        if (act[k]) {
+          row_offsets(g, r, &xo, &oo[k]);
+          q[k] = __ldcs(reinterpret_cast<const float4*>(x + xo) + lane_in_row);
+        }
+      }
+#pragma unroll
+      for (int k = 0; k < R; k++) {
+        uint64_t best = 0;
+        if (act[k]) {
+          const uint64_t i = lane_in_row * 4;
+          uint64_t c0 = cand(key_of_bits(__float_as_uint(q[k].x)), i);
+          uint64_t c1 = cand(key_of_bits(__float_as_uint(q[k].y)), i + 1);
+          uint64_t c2 = cand(key_of_bits(__float_as_uint(q[k].z)), i + 2);
+          uint64_t c3 = cand(key_of_bits(__float_as_uint(q[k].w)), i + 3);
+          uint64_t m01 = c0 > c1 ? c0 : c1, m23 = c2 > c3 ? c2 : c3;
+          best = m01 > m23 ? m01 : m23;
+        }
+        for (int o = lpr / 2; o > 0; o >>= 1) {
+          uint64_t w = __shfl_xor_sync(0xffffffffu, best, o, lpr);
+          best = w > best ? w : best;
+        }
+        if (act[k] && lane_in_row == 0) out[oo[k]] = 0xffffffffu - (uint32_t)best;
+      }
+    }
+    return;
+  }
   for (uint64_t r0 = (uint64_t)blockIdx.x * rows_per_block; r0 < g.rows; r0 += row_stride) {
     const uint64_t r = r0 + threadIdx.x / lpr;
     const bool active = r < g.rows;
@@ -276,6 +321,19 @@ lc_status lc_encode_argmax_rows(lc_context* ctx, void* stream, const lc_view* xp
     g.shape[d] = out.shape[d];
     g.xs[d] = x.strides[d];
     g.os[d] = out.strides[d];
+  }
+  // leading axes that step uniformly in both x and out (row r at r * stride) collapse to one
+  {
+    bool uniform = out.rank >= 1;
+    for (int d = 0; d + 1 < out.rank && uniform; d++)
+      if (x.strides[d] != x.strides[d + 1] * out.shape[d + 1] || out.strides[d] != out.strides[d + 1] * out.shape[d + 1])
+        uniform = false;
+    if (uniform && out.rank > 1) {
+      g.rank = 1;
+      g.shape[0] = g.rows;
+      g.xs[0] = x.strides[out.rank - 1];
+      g.os[0] = out.strides[out.rank - 1];
+    }
   }
   bool vec = g.col_stride == 1 && cols % 4 == 0 && (reinterpret_cast<uintptr_t>(x.data) + x.offset * 4) % 16 == 0;
   for (int d = 0; d < out.rank && vec; d++)

@@ -243,6 +243,32 @@ def test_argmax_rows_strided_and_odd(ctx):
     assert (out.cpu().numpy() == want).all()
 
 
+@pytest.mark.parametrize("rows,cols,offset", [(7, 33, 0), (5, 64, 0), (3, 200, 0), (9, 1000, 0), (6, 96, 1)])
+def test_argmax_rows_wide_and_misaligned(ctx, rows, cols, offset):
+    """Rows wider than the 16 lanes that share one (several loads per lane), odd widths and a
+    misaligned start (no 16-byte loads): ties across lanes, zero rows, NaN and infinities must
+    give the reference's indices."""
+    x = data.normal(rows * cols + offset, (rows, cols))
+    x[0, :] = 0.0                                   # all zero: index 0
+    if rows > 1:
+        x[1, cols - 1] = 7.5
+        x[1, 3] = -7.5                              # |x| tie across lanes: lowest index
+    if rows > 2:
+        x[2, cols // 2] = np.nan
+        x[2, 1] = np.inf                            # NaN outranks inf
+    if rows > 3:
+        x[3, :] = np.nan                            # all NaN: index 0
+    if rows > 4:
+        x[4, cols - 2] = -np.inf
+    flat = np.concatenate([np.zeros(offset, np.float32), x.ravel()])
+    t = dev(flat)
+    v = lb.View.raw(t, offset, [rows, cols], [cols, 1])
+    out = torch.empty((rows,), dtype=torch.uint32, device="cuda")
+    lb.argmax_rows(ctx, v, out)
+    want = O.argmax_rows(x)
+    assert (out.cpu().numpy() == want).all(), (out.cpu().numpy(), want)
+
+
 # ------------------------------------------------------------------------------------------------
 # contraction
 # ------------------------------------------------------------------------------------------------
