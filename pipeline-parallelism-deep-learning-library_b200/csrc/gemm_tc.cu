@@ -68,14 +68,15 @@ struct KParams {
 
 constexpr int kSmemMax = 232448;  // dynamic shared memory a CTA may opt in to on sm_100
 
-template <int BN, bool TF32X3, bool PAIR = false>
+template <int BN, bool TF32X3, bool PAIR = false, bool TWO_SM = false>
 struct Cfg {
   static constexpr int EPR = TF32X3 ? 32 : 64;             // elements per 128-byte row
   static constexpr int BK = EPR;                           // K per stage
   static constexpr int UMMA_K = TF32X3 ? 8 : 16;           // K per instruction (32 bytes)
   static constexpr int KSTEPS = BK / UMMA_K;               // 4
   static constexpr int A_BYTES = kBM * kRowBytes;          // 16 KiB
-  static constexpr int B_BYTES = BN * kRowBytes;
+  // TWO_SM: each CTA of the pair holds half of the tile's BN rows of B^T
+  static constexpr int B_BYTES = (TWO_SM ? BN / 2 : BN) * kRowBytes;
   static constexpr int STAGE_BYTES = (A_BYTES + B_BYTES) * (TF32X3 ? 2 : 1);
   // PAIR: the peer's raw partial of this CTA's column half lands here (f32, 128 x BN/2)
   static constexpr int RECV_BYTES = PAIR ? kBM * (BN / 2) * 4 : 0;
@@ -98,6 +99,7 @@ struct Cfg {
   static_assert(STAGES >= 2, "at least two stages");
   static_assert(SMEM <= kSmemMax, "shared memory budget");
   static_assert(!PAIR || (!TF32X3 && BN <= 128), "CTA pairs: 16-bit inputs, BN <= 128");
+  static_assert(!TWO_SM || (!TF32X3 && !PAIR && BN == 256), "2-SM products: 16-bit inputs, BN = 256");
 };
 
 __device__ __forceinline__ void unit_coords(const KParams& p, int32_t u, int32_t* b, int32_t* split, int32_t* tm,
@@ -584,9 +586,12 @@ __device__ __forceinline__ bool wait_counter(const int* counter, int target, int
   return true;
 }
 
-template <int BN, bool TF32X3, int EPI, bool PAIR, class Src>
+// TWO_SM: the 256-row tile of a unit is computed by a cluster of 2 CTAs with cta_group::2 MMAs
+// (rows 128 * rank .. + 127 of the tile live in CTA rank's TMEM); a unit is one output tile and
+// the pair walks the units together.
+template <int BN, bool TF32X3, int EPI, bool PAIR, class Src, bool TWO_SM = false>
 __device__ __forceinline__ void gemm_body(const Src& src) {
-  using C = Cfg<BN, TF32X3, PAIR>;
+  using C = Cfg<BN, TF32X3, PAIR, TWO_SM>;
   int* const err = src.kp(0).err;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
@@ -621,7 +626,7 @@ __device__ __forceinline__ void gemm_body(const Src& src) {
     }
     for (int a = 0; a < 2; a++) {
       lcd::mbar_init(&tfull[a], 1);
-      lcd::mbar_init(&tempty[a], 128);
+      lcd::mbar_init(&tempty[a], TWO_SM ? 256 : 128);  // 2-SM: both CTAs' epilogue threads, on the leader
     }
     lcd::mbar_init(drain, 1);
     lcd::mbar_init(recv_full, 128);
@@ -630,8 +635,13 @@ __device__ __forceinline__ void gemm_body(const Src& src) {
     lcd::fence_mbar_init();
   }
   if (warp == 1) {
-    lcd::tmem_alloc(tmem_slot, C::TMEM_COLS);
-    lcd::tmem_relinquish();
+    if constexpr (TWO_SM) {
+      lcd::tmem_alloc_2sm(tmem_slot, C::TMEM_COLS);
+      lcd::tmem_relinquish_2sm();
+    } else {
+      lcd::tmem_alloc(tmem_slot, C::TMEM_COLS);
+      lcd::tmem_relinquish();
+    }
   }
   if (warp == 0 && lane == 0) {
     for (int l = 0; l < src.layers(); l++) {
@@ -644,13 +654,19 @@ __device__ __forceinline__ void gemm_body(const Src& src) {
   lcd::tc_fence_after();
   const uint32_t tmem_base = *tmem_slot;
   // both CTAs of a pair have initialised their barriers before either arrives on the other's
-  if constexpr (PAIR) lcd::cluster_sync();
-  const uint32_t rank = PAIR ? lcd::cluster_ctarank() : 0u;
+  if constexpr (PAIR || TWO_SM) lcd::cluster_sync();
+  const uint32_t rank = (PAIR || TWO_SM) ? lcd::cluster_ctarank() : 0u;
+  // the units this CTA walks: every CTA on its own, or (TWO_SM) the pair together
+  const int32_t u_first = TWO_SM ? (int32_t)(blockIdx.x >> 1) : (int32_t)blockIdx.x;
+  const int32_t u_step = TWO_SM ? (int32_t)(gridDim.x >> 1) : (int32_t)gridDim.x;
+  // first C row of a unit's tile row tm held by this CTA
+  auto tile_row0 = [&](int32_t tm) -> int32_t { return TWO_SM ? tm * 256 + (int32_t)rank * 128 : tm * kBM; };
   // Programmatic dependent launch: the next kernel on the stream may start its own set-up now.
   // Everything below that reads or writes global memory first waits for the previous kernel.
   lcd::griddep_launch_dependents();
 
-  constexpr uint32_t kStageTx = C::A_BYTES + C::B_BYTES;
+  // bytes one stage's full barrier waits for (TWO_SM: both CTAs' loads land on the leader's)
+  constexpr uint32_t kStageTx = (C::A_BYTES + C::B_BYTES) * (TWO_SM ? 2 : 1);
 
   if (warp == 0) {
     if (lane == 0) {
@@ -661,6 +677,7 @@ __device__ __forceinline__ void gemm_body(const Src& src) {
       // the gate into up to STAGES slots and only the B loads wait.
       const uint64_t once = lcd::policy_evict_first();
       const uint64_t keep = lcd::policy_evict_last();
+      const uint64_t normal = lcd::policy_evict_normal();
       int s = 0;
       uint32_t ph = 0;
       uint32_t filled = 0, last_par = 0;  // bit s: stage s filled at least once / parity of its last fill
@@ -685,17 +702,26 @@ __device__ __forceinline__ void gemm_body(const Src& src) {
         int32_t pend[C::STAGES][4];
         int npend = 0;
         auto load = [&](int st, void* dst, const CUtensorMap* map, int32_t c0, int32_t c1, int32_t b, bool hint) {
-          if (hint) lcd::tma_load_3d_hint(dst, map, &full[st], c0, c1, b, once);
-          else if (EPI == 2) lcd::tma_load_3d_hint(dst, map, &full[st], c0, c1, b, keep);
-          else lcd::tma_load_3d(dst, map, &full[st], c0, c1, b);
+          if constexpr (TWO_SM) {
+            // bytes count on the leader's barrier for this stage
+            lcd::tma_load_3d_2sm(dst, map, lcd::leader_addr(lcd::smem_u32(&full[st])), c0, c1, b,
+                                 hint ? once : (EPI == 2 ? keep : normal));
+          } else {
+            if (hint) lcd::tma_load_3d_hint(dst, map, &full[st], c0, c1, b, once);
+            else if (EPI == 2) lcd::tma_load_3d_hint(dst, map, &full[st], c0, c1, b, keep);
+            else lcd::tma_load_3d(dst, map, &full[st], c0, c1, b);
+          }
         };
+        // this CTA's rows of the B^T tile: all BN, or (TWO_SM) its half
+        constexpr int kBRows = TWO_SM ? BN / 2 : BN;
+        const int32_t b_row_off = TWO_SM ? (int32_t)rank * kBRows : 0;
         auto load_b = [&](int st, int32_t k0, int32_t tn, int32_t b) {
           if (!p.b_mn) {
-            load(st, b_hi(st), tb, k0, tn * BN, b, p.b_once);
+            load(st, b_hi(st), tb, k0, tn * BN + b_row_off, b, p.b_once);
           } else {
 #pragma unroll
-            for (int j = 0; j < BN / C::EPR; j++)
-              load(st, b_hi(st) + j * (C::BK * kRowBytes), tb, tn * BN + j * C::EPR, k0, b, p.b_once);
+            for (int j = 0; j < kBRows / C::EPR; j++)
+              load(st, b_hi(st) + j * (C::BK * kRowBytes), tb, tn * BN + b_row_off + j * C::EPR, k0, b, p.b_once);
           }
         };
         auto release = [&]() -> bool {
@@ -705,11 +731,12 @@ __device__ __forceinline__ void gemm_body(const Src& src) {
           open = true;
           return true;
         };
-        for (int32_t u = blockIdx.x; ok && u < p.units; u += gridDim.x) {
+        for (int32_t u = u_first; ok && u < p.units; u += u_step) {
           int32_t b, split, tm, tn;
           unit_coords(p, u, &b, &split, &tm, &tn);
           const int32_t kb = split * p.kt_per_split;
           const int32_t ke = min(kb + p.kt_per_split, p.k_tiles);
+          const int32_t a_row0 = tile_row0(tm);
           for (int32_t kt = kb; kt < ke; kt++) {
             // every slot holds an A tile waiting for its B: open the gate before reusing one
             if (!open && npend == C::STAGES && !release()) {
@@ -720,14 +747,16 @@ __device__ __forceinline__ void gemm_body(const Src& src) {
               ok = false;
               break;
             }
-            lcd::mbar_arrive_expect_tx(&full[s], kStageTx);
+            // TWO_SM: only the leader arms the stage (with both CTAs' bytes); the peer's loads
+            // may land first, which an mbarrier allows while its arrival is still pending
+            if (!TWO_SM || rank == 0) lcd::mbar_arrive_expect_tx(&full[s], kStageTx);
             const int32_t k0 = kt * C::BK;
             if (!p.a_mn) {
-              load(s, a_hi(s), ta, k0, tm * kBM, b, p.a_once);
+              load(s, a_hi(s), ta, k0, a_row0, b, p.a_once);
             } else {
 #pragma unroll
               for (int j = 0; j < kBM / C::EPR; j++)
-                load(s, a_hi(s) + j * (C::BK * kRowBytes), ta, tm * kBM + j * C::EPR, k0, b, p.a_once);
+                load(s, a_hi(s) + j * (C::BK * kRowBytes), ta, a_row0 + j * C::EPR, k0, b, p.a_once);
             }
             if (open) {
               load_b(s, k0, tn, b);
@@ -749,13 +778,16 @@ __device__ __forceinline__ void gemm_body(const Src& src) {
         // a product with fewer k-tiles than stages (or none for this CTA) still opens its gate
         if (ok && !open && !release()) ok = false;
       }
-      // never leave a bulk copy in flight into shared memory that is about to be released
-      for (int t = 0; t < C::STAGES; t++)
-        if (filled & (1u << t)) lcd::mbar_wait(&full[t], (last_par >> t) & 1u, err);
+      // never leave a bulk copy in flight into shared memory that is about to be released (the
+      // 2-SM peer's copies complete on the leader's barriers; the closing cluster barrier covers
+      // them, as the leader waits here first)
+      if (!TWO_SM || rank == 0)
+        for (int t = 0; t < C::STAGES; t++)
+          if (filled & (1u << t)) lcd::mbar_wait(&full[t], (last_par >> t) & 1u, err);
     }
   } else if (warp == 1) {
-    if (lane == 0) {
-      // ---------------- MMA issuer ----------------
+    if (lane == 0 && (!TWO_SM || rank == 0)) {
+      // ---------------- MMA issuer (TWO_SM: the leader, for both CTAs) ----------------
       // The accumulator is handed to the epilogue every KC k-tiles (a "chunk"): once per unit for
       // 16-bit inputs, every kChunkTiles k-tiles for 3xTF32, whose long sums the epilogue then
       // adds with round-to-nearest (the tensor core's own f32 accumulation truncates).
@@ -765,7 +797,7 @@ __device__ __forceinline__ void gemm_body(const Src& src) {
       bool ok = true;
       for (int l = 0; ok && l < src.layers(); l++) {
       decltype(auto) p = src.kp(l);  // a chain's are copied to registers once per product
-      for (int32_t u = blockIdx.x; ok && u < p.units; u += gridDim.x) {
+      for (int32_t u = u_first; ok && u < p.units; u += u_step) {
         int32_t b, split, tm, tn;
         unit_coords(p, u, &b, &split, &tm, &tn);
         (void)b;
@@ -815,23 +847,28 @@ __device__ __forceinline__ void gemm_body(const Src& src) {
               lcd::umma_tf32(d_tmem, dal, db, p.idesc, accum);  // lo(A) * hi(B)
               lcd::umma_tf32(d_tmem, da, dbl, p.idesc, 1u);     // hi(A) * lo(B)
               lcd::umma_tf32(d_tmem, da, db, p.idesc, 1u);      // hi(A) * hi(B)
+            } else if constexpr (TWO_SM) {
+              lcd::umma_f16_2sm(d_tmem, da, db, p.idesc, accum);
             } else {
               lcd::umma_f16(d_tmem, da, db, p.idesc, accum);
             }
           }
-          lcd::umma_commit(&empty[s]);
+          if constexpr (TWO_SM) lcd::umma_commit_2sm_both(&empty[s]);  // frees the stage in both CTAs
+          else lcd::umma_commit(&empty[s]);
           if (++s == C::STAGES) {
             s = 0;
             ph ^= 1u;
           }
         }
         if (!ok) break;
-        lcd::umma_commit(&tfull[acc]);
+        if constexpr (TWO_SM) lcd::umma_commit_2sm_both(&tfull[acc]);
+        else lcd::umma_commit(&tfull[acc]);
         }
       }
       }
       // every MMA this thread issued has retired before TMEM is released
-      lcd::umma_commit(drain);
+      if constexpr (TWO_SM) lcd::umma_commit_2sm(drain);
+      else lcd::umma_commit(drain);
       lcd::mbar_wait(drain, 0, err);
     }
   } else if (warp < 6) {
@@ -845,16 +882,16 @@ __device__ __forceinline__ void gemm_body(const Src& src) {
     for (int l = 0; ok && l < src.layers(); l++) {
     decltype(auto) p = src.kp(l);  // a chain's are copied to registers once per product
     const bool split_mode = p.splits > 1 && !PAIR;
-    for (int32_t u = blockIdx.x; ok && u < p.units; u += gridDim.x) {
+    for (int32_t u = u_first; ok && u < p.units; u += u_step) {
       int32_t b, split, tm, tn;
       unit_coords(p, u, &b, &split, &tm, &tn);
-      const int32_t m = tm * kBM + q * 32 + lane;
+      const int32_t m = tile_row0(tm) + q * 32 + lane;
       const int64_t c_row = p.c_off + (int64_t)b * p.c_bs + (int64_t)m * p.c_ms;
       // one 32-column group [n0, n0 + 32) of this lane's row, straight from the tcgen05.ld registers
       // (warp-uniform branches: n0, cnt and the block's row count are the same for all lanes)
       auto emit = [&](const uint32_t (&r)[32], int32_t n0) {
         const int32_t cnt = min(32, p.N - n0);
-        const int32_t m0w = tm * kBM + q * 32;
+        const int32_t m0w = tile_row0(tm) + q * 32;
         const int32_t rows = min(32, p.M - m0w);
         if (cnt <= 0 || rows <= 0) return;
         float v[32];
@@ -1011,10 +1048,10 @@ __device__ __forceinline__ void gemm_body(const Src& src) {
         lcd::tc_fence_after();
         // The epilogue's reads (master weights, mask, old C) wait on HBM group after group; pull
         // the next unit's rows into L2 now, a tile ahead, so that they come from L2 then.
-        if (!split_mode && p.vec && (EPI != 0 || p.beta != 0.0f) && u + (int32_t)gridDim.x < p.units) {
+        if (!split_mode && p.vec && (EPI != 0 || p.beta != 0.0f) && u + u_step < p.units) {
           int32_t b2, s2, tm2, tn2;
-          unit_coords(p, u + (int32_t)gridDim.x, &b2, &s2, &tm2, &tn2);
-          const int32_t m2 = tm2 * kBM + q * 32 + lane;
+          unit_coords(p, u + u_step, &b2, &s2, &tm2, &tn2);
+          const int32_t m2 = tile_row0(tm2) + q * 32 + lane;
           const int32_t n2 = tn2 * BN;
           if (m2 < p.M && n2 < p.N) {
             const int es = (EPI == 2 || p.c_dtype == LC_F32) ? 4 : 2;
@@ -1032,7 +1069,9 @@ __device__ __forceinline__ void gemm_body(const Src& src) {
           emit(r, tn * BN + g * 32);
         }
         lcd::tc_fence_before();
-        lcd::mbar_arrive(&tempty[acc]);
+        // TWO_SM: the leader's MMAs refill both CTAs' accumulators, so both release on its barrier
+        if (TWO_SM && rank == 1) lcd::mbar_arrive_remote(lcd::leader_addr(lcd::smem_u32(&tempty[acc])));
+        else lcd::mbar_arrive(&tempty[acc]);
         h++;
       }
       if (split_mode && p.fixup) {
@@ -1131,9 +1170,12 @@ __device__ __forceinline__ void gemm_body(const Src& src) {
   }
 
   __syncthreads();
+  // 2-SM: the peer's TMEM is written by the leader's MMAs; free it only once both CTAs are done
+  if constexpr (TWO_SM) lcd::cluster_sync();
   if (warp == 1) {
     lcd::tc_fence_after();
-    lcd::tmem_dealloc(tmem_base, C::TMEM_COLS);
+    if constexpr (TWO_SM) lcd::tmem_dealloc_2sm(tmem_base, C::TMEM_COLS);
+    else lcd::tmem_dealloc(tmem_base, C::TMEM_COLS);
   }
   // neither CTA of a pair leaves while the other may still access its shared memory
   if constexpr (PAIR) lcd::cluster_sync();
@@ -1144,6 +1186,14 @@ __global__ void __launch_bounds__(Cfg<BN, TF32X3, PAIR>::THREADS, 1)
     gemm_tc_kernel(const __grid_constant__ CUtensorMap tma_a, const __grid_constant__ CUtensorMap tma_b,
                    const __grid_constant__ KParams p) {
   gemm_body<BN, TF32X3, EPI, PAIR>(OneProduct{&tma_a, &tma_b, &p});
+}
+
+// 256 x 256 tiles over a cluster of 2 CTAs with cta_group::2 MMAs (16-bit inputs, no split).
+template <int EPI>
+__global__ void __launch_bounds__(Cfg<256, false, false, true>::THREADS, 1)
+    gemm_2sm_kernel(const __grid_constant__ CUtensorMap tma_a, const __grid_constant__ CUtensorMap tma_b,
+                    const __grid_constant__ KParams p) {
+  gemm_body<256, false, EPI, false, OneProduct, true>(OneProduct{&tma_a, &tma_b, &p});
 }
 
 // A chain of skinny products (BN = 64, 16-bit inputs, CTA pairs): the pipeline's layer loop of
@@ -1379,6 +1429,74 @@ lc_status launch_kernel(lc_context* ctx, cudaStream_t s, const CUtensorMap& ta, 
   return LC_OK;
 }
 
+template <int EPI>
+cudaLaunchConfig_t launch_config_2sm(cudaStream_t s, int grid, cudaLaunchAttribute (&at)[2]) {
+  using C = Cfg<256, false, false, true>;
+  cudaLaunchConfig_t cfg{};
+  cfg.gridDim = dim3((unsigned)grid);
+  cfg.blockDim = dim3(C::THREADS);
+  cfg.dynamicSmemBytes = C::SMEM;
+  cfg.stream = s;
+  at[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  at[0].val.programmaticStreamSerializationAllowed = 1;
+  at[1].id = cudaLaunchAttributeClusterDimension;
+  at[1].val.clusterDim.x = 2;
+  at[1].val.clusterDim.y = 1;
+  at[1].val.clusterDim.z = 1;
+  cfg.attrs = at;
+  cfg.numAttrs = 2;
+  return cfg;
+}
+
+template <int EPI>
+lc_status prepare_2sm(lc_context* ctx) {
+  static bool attr_set[64] = {false};
+  if (!attr_set[ctx->device % 64]) {
+    cudaError_t e = cudaFuncSetAttribute(gemm_2sm_kernel<EPI>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                         Cfg<256, false, false, true>::SMEM);
+    if (e != cudaSuccess) return lc::cuda_fail(e, "cudaFuncSetAttribute(gemm 2sm)");
+    attr_set[ctx->device % 64] = true;
+  }
+  return LC_OK;
+}
+
+// How many 2-SM clusters fit on the device at once (0 when they cannot launch).
+template <int EPI>
+int capacity_2sm(lc_context* ctx) {
+  static int cap[64];
+  static bool known[64] = {false};
+  const int d = ctx->device % 64;
+  if (!known[d]) {
+    int n = 0;
+    if (prepare_2sm<EPI>(ctx) == LC_OK) {
+      cudaLaunchAttribute at[2];
+      cudaLaunchConfig_t cfg = launch_config_2sm<EPI>(nullptr, 2, at);
+      if (cudaOccupancyMaxActiveClusters(&n, gemm_2sm_kernel<EPI>, &cfg) != cudaSuccess) {
+        cudaGetLastError();
+        n = 0;
+      }
+    }
+    cap[d] = n;
+    known[d] = true;
+  }
+  return cap[d];
+}
+
+template <int EPI>
+lc_status launch_2sm(lc_context* ctx, cudaStream_t s, const CUtensorMap& ta, const CUtensorMap& tb, const KParams& p,
+                     int grid) {
+  lc_status st = prepare_2sm<EPI>(ctx);
+  if (st) return st;
+  cudaLaunchAttribute at[2];
+  cudaLaunchConfig_t cfg = launch_config_2sm<EPI>(s, grid, at);
+  cudaError_t e = cudaLaunchKernelEx(&cfg, gemm_2sm_kernel<EPI>, ta, tb, p);
+  lc::record_launch(ctx, "gemm_bf16_2sm_n256");
+  if (e != cudaSuccess) return lc::cuda_fail(e, "gemm 2sm launch");
+  e = cudaGetLastError();
+  if (e != cudaSuccess) return lc::cuda_fail(e, "gemm 2sm launch");
+  return LC_OK;
+}
+
 int64_t ceil_div(int64_t a, int64_t b) { return (a + b - 1) / b; }
 
 }  // namespace
@@ -1411,8 +1529,8 @@ struct Planned {
   KParams p{};
   CUtensorMap ta, tb;
   int bn = 64;
-  bool tf32x3 = false, pair = false;
-  int64_t pair_clusters = 0, tiles = 0, units = 0, splits = 1, M = 0, N = 0;
+  bool tf32x3 = false, pair = false, two_sm = false;
+  int64_t pair_clusters = 0, two_sm_clusters = 0, tiles = 0, units = 0, splits = 1, M = 0, N = 0;
 };
 
 lc_status plan_gemm(lc_context* ctx, const lc::GemmProblem& pr, lc_contract_plan* plan, bool dry_run, Planned* out) {
@@ -1482,6 +1600,24 @@ lc_status plan_gemm(lc_context* ctx, const lc::GemmProblem& pr, lc_contract_plan
     pair_clusters = std::min<int64_t>({tiles, (int64_t)cap, (ctx->sm_count - pr.reserve_sms) / 2});
   }
   const bool pair = pair_clusters > 0;
+  // 256-row tiles over CTA pairs (cta_group::2 MMAs): each CTA reads 128 rows of A and half of
+  // the tile's B^T, a third less operand traffic per output than a 128 x 256 tile on one SM.
+  // Taken for unsplit BN = 256 products with enough tiles to give every pair of SMs work.
+  static const bool env_no_2sm = [] {
+    const char* e = getenv("LC_GEMM_2SM");  // tuning override: "0" keeps 128-row tiles on one SM
+    return e != nullptr && e[0] == '0';
+  }();
+  const int64_t tiles_m2 = ceil_div(M, 256);
+  const int64_t tiles2 = tiles_m2 * tiles_n * pr.batch;
+  const int64_t sm_pairs = (ctx->sm_count - pr.reserve_sms) / 2;
+  int64_t two_sm_clusters = 0;
+  if (!dry_run && !tf32x3 && !pair && splits == 1 && bn == 256 && M >= 256 && tiles2 >= sm_pairs && !env_no_2sm) {
+    const int cap = pr.epi == 0 ? capacity_2sm<0>(ctx) : pr.epi == 1 ? capacity_2sm<1>(ctx) : capacity_2sm<2>(ctx);
+    two_sm_clusters = std::min<int64_t>({tiles2, (int64_t)cap, sm_pairs});
+  }
+  const bool two_sm = two_sm_clusters > 0;
+  const int64_t tiles_m_eff = two_sm ? tiles_m2 : tiles_m;
+  const int64_t units_eff = two_sm ? tiles2 : units;
   if (units >= (1ll << 31) || k_tiles >= (1ll << 31)) return fail(LC_ERR_INVALID_ARGUMENT, "problem too large");
 
   if (operand_major(A) < 0 || operand_major(B) < 0) return fail(LC_ERR_INVALID_ARGUMENT, "operand has no unit stride");
@@ -1518,7 +1654,7 @@ lc_status plan_gemm(lc_context* ctx, const lc::GemmProblem& pr, lc_contract_plan
   if (st) return st;
   if (!b_mn) {
     uint64_t rs = B.mn > 1 ? B.mn_stride * es : ((B.k * es + 15) / 16) * 16;
-    st = make_map(&tb, bbase, pr.in_dtype, B.k, B.mn, pr.batch, rs, bstride(B, rs * B.mn), epr, bn);
+    st = make_map(&tb, bbase, pr.in_dtype, B.k, B.mn, pr.batch, rs, bstride(B, rs * B.mn), epr, two_sm ? bn / 2 : bn);
   } else {
     uint64_t rs = B.k > 1 ? B.k_stride * es : ((B.mn * es + 15) / 16) * 16;
     st = make_map(&tb, bbase, pr.in_dtype, B.mn, B.k, pr.batch, rs, bstride(B, rs * B.k), epr, epr, tf32x3);
@@ -1533,20 +1669,20 @@ lc_status plan_gemm(lc_context* ctx, const lc::GemmProblem& pr, lc_contract_plan
   p.kt_per_split = (int32_t)kps;
   p.splits = (int32_t)splits;
   p.batch = (int32_t)pr.batch;
-  p.tiles_m = (int32_t)tiles_m;
+  p.tiles_m = (int32_t)tiles_m_eff;
   p.tiles_n = (int32_t)tiles_n;
-  p.units = (int32_t)units;
+  p.units = (int32_t)units_eff;
   p.split_minor = pair ? 1 : 0;
   static const bool env_no_hint = [] {
     const char* e = getenv("LC_GEMM_EVICT_FIRST");  // tuning override: "0" drops the streaming hint
     return e != nullptr && e[0] == '0';
   }();
   p.a_once = (tiles_n == 1 && !env_no_hint) ? 1 : 0;
-  p.b_once = (tiles_m == 1 && !env_no_hint) ? 1 : 0;
+  p.b_once = (tiles_m_eff == 1 && !env_no_hint) ? 1 : 0;
   p.a_mn = a_mn;
   p.b_mn = b_mn;
   const uint32_t fmt = tf32x3 ? 2u : (pr.in_dtype == LC_BF16 ? 1u : 0u);
-  p.idesc = lcd::make_idesc(fmt, 128, bn, a_mn, b_mn);
+  p.idesc = lcd::make_idesc(fmt, two_sm ? 256 : 128, bn, a_mn, b_mn);
   p.c_dtype = pr.c_dtype;
   p.relu = pr.relu;
   p.c = pr.c;
@@ -1576,8 +1712,10 @@ lc_status plan_gemm(lc_context* ctx, const lc::GemmProblem& pr, lc_contract_plan
   out->tf32x3 = tf32x3;
   out->pair = pair;
   out->pair_clusters = pair_clusters;
-  out->tiles = tiles;
-  out->units = units;
+  out->two_sm = two_sm;
+  out->two_sm_clusters = two_sm_clusters;
+  out->tiles = two_sm ? tiles2 : tiles;
+  out->units = units_eff;
   out->splits = splits;
   out->M = (int64_t)M;
   out->N = (int64_t)N;
@@ -1663,8 +1801,13 @@ lc_status gemm_run(lc_context* ctx, cudaStream_t s, const GemmProblem& pr, lc_co
     }
   }
   const int grid = pair ? (int)(2 * pair_clusters)
-                        : (int)std::max<int64_t>(1, std::min<int64_t>(units, ctx->sm_count - pr.reserve_sms));
-  if (pair) {
+                   : pl.two_sm ? (int)(2 * pl.two_sm_clusters)
+                               : (int)std::max<int64_t>(1, std::min<int64_t>(units, ctx->sm_count - pr.reserve_sms));
+  if (pl.two_sm) {
+    st = pr.epi == 0   ? launch_2sm<0>(ctx, s, ta, tb, p, grid)
+         : pr.epi == 1 ? launch_2sm<1>(ctx, s, ta, tb, p, grid)
+                       : launch_2sm<2>(ctx, s, ta, tb, p, grid);
+  } else if (pair) {
     st = bn == 64 ? (pr.epi == 0 ? launch_kernel<64, false, 0, true>(ctx, s, ta, tb, p, grid)
                                  : launch_kernel<64, false, 1, true>(ctx, s, ta, tb, p, grid))
                   : (pr.epi == 0 ? launch_kernel<128, false, 0, true>(ctx, s, ta, tb, p, grid)

@@ -21,11 +21,12 @@ def main():
     L, d, mb, mbs, lr, steps = cfg["layers"], cfg["width"], cfg["microbatch"], cfg["microbatches"], cfg["lr"], cfg["steps"]
     p = Pipeline(L, d, mb, mbs, lr=lr, rank=rank, world=world, device=rank, uid=uid, timeout_ms=60000)
     p.init_weights(cfg["seed"], d ** -0.5)
+    w0 = {f"w0_{p.first + i}": p.get_weight(i) for i in range(p.count)}
     x = data.normal(1, (mb * mbs, d)) if rank == 0 else None
     t = data.normal(2, (mb * mbs, d)) if rank == world - 1 else None
     losses = [p.step(x, t) for _ in range(steps)]
     ws = {f"w{p.first + i}": p.get_weight(i) for i in range(p.count)}
-    np.savez(out, losses=np.array(losses, dtype=np.float32), **ws)
+    np.savez(out, losses=np.array(losses, dtype=np.float32), **ws, **w0)
     p.close()
 
 

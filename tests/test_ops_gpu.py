@@ -348,6 +348,17 @@ def test_contract_bf16(ctx, m, n, k):
     assert rel <= BF16_TOL, rel
 
 
+@pytest.mark.parametrize("m,n,k,bt,dtype", [(2304, 2304, 512, False, torch.bfloat16),
+                                             (2400, 2560, 256, True, torch.bfloat16),
+                                             (2560, 2304, 320, False, torch.float16)])
+def test_contract_two_sm_tiles(ctx, m, n, k, bt, dtype):
+    """Products with a 256 x 256 tile for every pair of SMs run on CTA pairs with cta_group::2
+    MMAs (each CTA holds 128 rows of A and half of B^T): both B layouts, an M tail, f16."""
+    rel, *_ = run_gemm_case(ctx, m, n, k, dtype=dtype, bt=bt, seed=m + k)
+    assert rel <= BF16_TOL, rel
+    assert "gemm_bf16_2sm_n256" in ctx.debug_launches()[-4:]
+
+
 def test_contract_layouts_and_scalars(ctx):
     for at, bt in ((True, False), (False, True), (True, True)):
         rel, *_ = run_gemm_case(ctx, 96, 80, 72, at=at, bt=bt, seed=3)

@@ -133,3 +133,31 @@ def test_layer_chains_equal_one_launch_per_layer(gpu, tmp_path):
     assert a["losses"][1] < a["losses"][0]
     for l in range(cfg["layers"]):
         assert a[f"w{l}"].tobytes() == b[f"w{l}"].tobytes(), l
+
+
+def test_weight_update_on_two_sm_tiles(gpu, tmp_path):
+    """At width 2304 the weight-gradient product has a 256 x 256 tile for every pair of SMs and
+    runs on CTA pairs with cta_group::2 MMAs and the fused SGD; the update must match the one-SM
+    kernel's (LC_GEMM_2SM=0) to within the rounding of a differently ordered f32 accumulation."""
+    import os
+    import subprocess
+    import sys
+    here = Path(__file__).resolve().parent
+    cfg = {"layers": 2, "width": 2304, "microbatch": 64, "microbatches": 2, "lr": 1e-1, "steps": 1, "seed": 9,
+           "rank": 0, "world": 1, "uid": ""}
+    outs = {}
+    for mode in ("two_sm", "one_sm"):
+        env = dict(os.environ)
+        if mode == "one_sm":
+            env["LC_GEMM_2SM"] = "0"
+        c = dict(cfg, out=str(tmp_path / f"{mode}.npz"))
+        r = subprocess.run([sys.executable, str(here / "_pipeline_rank.py"), json.dumps(c)], env=env,
+                           capture_output=True, text=True, timeout=600)
+        assert r.returncode == 0, r.stdout + r.stderr
+        outs[mode] = np.load(tmp_path / f"{mode}.npz")
+    a, b = outs["two_sm"], outs["one_sm"]
+    assert a["losses"].tobytes() == b["losses"].tobytes()  # the forward precedes any update
+    for l in range(cfg["layers"]):
+        step = np.abs(a[f"w{l}"] - a[f"w0_{l}"]).max()
+        assert step > 0
+        assert np.abs(a[f"w{l}"] - b[f"w{l}"]).max() <= 1e-3 * step, l
