@@ -17,6 +17,7 @@
 #include <algorithm>
 #include <cstring>
 #include <string>
+#include <type_traits>
 
 #include "internal.h"
 
@@ -221,6 +222,63 @@ __global__ void __launch_bounds__(kThreads) argmax_rows_kernel(const float* __re
   }
 }
 
+// Rows of 16 to 512 floats (a power of two) in 16-byte aligned runs: L = cols / 16 lanes per
+// row, each lane 4 float4s at columns 4 * (lane + L * j), two rows per thread in flight (8 loads).
+// A lane scans its 16 values in increasing column order with a strict comparison, so it keeps the
+// lowest index among equal keys and tracks the winner as a position 0..15 that becomes a column
+// only once; NaN magnitudes clamp to 0x7f800001, above +inf and equal to one another, which
+// orders exactly like kNanKey.  Only log2(L) shuffle levels remain per row.
+template <int L>
+__global__ void __launch_bounds__(kThreads) argmax_rows_vec_kernel(const float* __restrict__ x,
+                                                                    uint32_t* __restrict__ out, RowGeom g) {
+  constexpr int W = 4, R = 2;
+  constexpr int kGroupRows = kThreads / L;  // rows per block per sub-pass
+  const uint32_t lane = threadIdx.x % L;
+  const uint64_t block_rows = (uint64_t)kGroupRows * R;
+  for (uint64_t r0 = (uint64_t)blockIdx.x * block_rows; r0 < g.rows; r0 += (uint64_t)gridDim.x * block_rows) {
+    float4 q[R][W];
+    uint64_t oo[R];
+    bool act[R];
+#pragma unroll
+    for (int k = 0; k < R; k++) {
+      const uint64_t r = r0 + (uint64_t)k * kGroupRows + threadIdx.x / L;
+      act[k] = r < g.rows;
+      uint64_t xo = 0;
+      oo[k] = 0;
+      if (act[k]) row_offsets(g, r, &xo, &oo[k]);
+      const float4* p = reinterpret_cast<const float4*>(x + xo) + lane;
+#pragma unroll
+      for (int j = 0; j < W; j++) q[k][j] = act[k] ? __ldcs(p + L * j) : make_float4(0.f, 0.f, 0.f, 0.f);
+    }
+#pragma unroll
+    for (int k = 0; k < R; k++) {
+      uint32_t bk = 0, bp = 0;
+#pragma unroll
+      for (int j = 0; j < W; j++) {
+        const float v[4] = {q[k][j].x, q[k][j].y, q[k][j].z, q[k][j].w};
+#pragma unroll
+        for (int e = 0; e < 4; e++) {
+          const uint32_t kk = min(__float_as_uint(v[e]) & 0x7fffffffu, 0x7f800001u);
+          if (j == 0 && e == 0) {
+            bk = kk;
+          } else if (kk > bk) {
+            bk = kk;
+            bp = (uint32_t)(4 * j + e);
+          }
+        }
+      }
+      const uint32_t col = 4 * (lane + L * (bp >> 2)) + (bp & 3);
+      uint64_t best = cand(bk, col);
+#pragma unroll
+      for (int o = L / 2; o > 0; o >>= 1) {
+        const uint64_t w = __shfl_xor_sync(0xffffffffu, best, o, L);
+        best = w > best ? w : best;
+      }
+      if (act[k] && lane == 0) out[oo[k]] = 0xffffffffu - (uint32_t)best;
+    }
+  }
+}
+
 lc_status check_out_one(const lc_view& out) {
   using namespace lc;
   if (out.dtype != LC_U32) return fail(LC_ERR_INVALID_ARGUMENT, "argmax output must be u32");
@@ -339,10 +397,40 @@ lc_status lc_encode_argmax_rows(lc_context* ctx, void* stream, const lc_view* xp
   for (int d = 0; d < out.rank && vec; d++)
     if (out.shape[d] > 1 && (x.strides[d] * 4) % 16 != 0) vec = false;
   g.vec = vec ? 1 : 0;
+  cudaStream_t s = stream_of(ctx, stream);
+  if (vec && cols >= 16 && cols <= 512 && (cols & (cols - 1)) == 0) {
+    const int L = (int)(cols / 16);
+    const uint64_t rows_per_pass = (uint64_t)(kThreads / L) * 2;
+    const float* xp = static_cast<const float*>(x.data);
+    uint32_t* op = static_cast<uint32_t*>(out.data);
+    // one wave of resident blocks, each looping over its share of the rows
+    auto launch = [&](auto lanes) {
+      constexpr int kL = decltype(lanes)::value;
+      static const int resident = [] {
+        int b = 0;
+        return cudaOccupancyMaxActiveBlocksPerMultiprocessor(&b, argmax_rows_vec_kernel<kL>, kThreads, 0) == cudaSuccess && b > 0
+                   ? b : 1;
+      }();
+      const uint64_t blocks = std::min<uint64_t>((g.rows + rows_per_pass - 1) / rows_per_pass,
+                                                 (uint64_t)ctx->sm_count * resident);
+      argmax_rows_vec_kernel<kL><<<(unsigned)std::max<uint64_t>(blocks, 1), kThreads, 0, s>>>(xp, op, g);
+    };
+    switch (L) {
+      case 1: launch(std::integral_constant<int, 1>{}); break;
+      case 2: launch(std::integral_constant<int, 2>{}); break;
+      case 4: launch(std::integral_constant<int, 4>{}); break;
+      case 8: launch(std::integral_constant<int, 8>{}); break;
+      case 16: launch(std::integral_constant<int, 16>{}); break;
+      default: launch(std::integral_constant<int, 32>{}); break;
+    }
+    record_launch(ctx, "argmax_rows");
+    cudaError_t e = cudaGetLastError();
+    if (e != cudaSuccess) return cuda_fail(e, "argmax_rows launch");
+    return LC_OK;
+  }
   int lpr = 1;
   const uint64_t per_lane_items = vec ? cols / 4 : cols;
   while (lpr < 32 && (uint64_t)lpr * 2 <= per_lane_items) lpr *= 2;
-  cudaStream_t s = stream_of(ctx, stream);
   const uint64_t rows_per_block = kThreads / lpr;
   const uint64_t blocks = std::min<uint64_t>((g.rows + rows_per_block - 1) / rows_per_block, (uint64_t)ctx->sm_count * 16);
   argmax_rows_kernel<<<(unsigned)std::max<uint64_t>(blocks, 1), kThreads, 0, s>>>(

@@ -492,8 +492,8 @@ __device__ __forceinline__ void store_partial(const KParams& p, const float (&v)
   }
 }
 
-// Sum of the splits' partials of 32 columns of one row, in split order from +0 (the order the
-// separate reduce kernel uses too, so the result does not depend on which path reduced).
+// Sum of the splits' partials of 32 columns of one row, in split order from +0 (for up to 8
+// splits the separate reduce kernel's order is this one too).
 __device__ __forceinline__ void sum_partials(const KParams& p, float (&v)[32], int32_t b, int32_t m, int32_t n0,
                                              int32_t cnt) {
 #pragma unroll
@@ -1204,24 +1204,44 @@ __global__ void __launch_bounds__(Cfg<64, false, true>::THREADS, 1)
   gemm_body<64, false, EPI, true>(ChainSrc{&cp});
 }
 
-// ---- split-K reduce for many splits: C = epilogue(sum_s partial[s]), splits summed in order -----
-// One thread per 4 consecutive columns of one row (16-byte partial loads); used when so many
-// splits share a tile that reducing inside the GEMM would serialise on a few warps.  Consecutive
-// threads take consecutive rows when C's kernel rows are its contiguous axis (the swapped skinny
-// products), consecutive column quads otherwise, so that C's stores coalesce either way.
+// ---- split-K reduce for many splits: C = epilogue(sum_s partial[s]) -------------------------------
+// Used when so many splits share a tile that reducing inside the GEMM would serialise on a few
+// warps.  kReduceChunks threads share each output quad (4 consecutive columns of one row,
+// 16-byte partial loads): thread g sums the run of splits [g * c, (g + 1) * c), c =
+// ceil(splits / kReduceChunks), in split order from +0 with its loads in flight ahead of the
+// adds, and the quad's total is the run sums added in run order from +0.  Eight threads per
+// quad keep a small output's partials in flight together; one thread walking all the splits
+// waited out an L2 round trip per kReduceDepth splits.  The order depends only on the split
+// count, so results are deterministic; up to kReduceChunks splits it is plain split order, the
+// in-kernel fixup's.  Consecutive quads take consecutive rows when C's kernel rows are its
+// contiguous axis (the swapped skinny products), consecutive column quads otherwise, so that
+// C's stores coalesce either way.
+constexpr int kReduceBlock = 128;
+constexpr int kReduceChunks = 8;
+
 template <int EPI>
-__global__ void __launch_bounds__(256) splitk_reduce_kernel(const KParams p) {
+__global__ void __launch_bounds__(kReduceBlock) splitk_reduce_kernel(const KParams p) {
+  constexpr int kReduceDepth = 16;
+  constexpr int kQuadsPerBlock = kReduceBlock / kReduceChunks;
+  lcd::griddep_launch_dependents();
+  lcd::griddep_wait();  // the partials are the GEMM's output
   const int32_t nq = (p.N + 3) / 4;  // column quads per row
   const int64_t rows = (int64_t)p.batch * p.M;
   const int64_t total = rows * nq;
   const int64_t plane = rows * (int64_t)p.N;
-  const int64_t stride = (int64_t)gridDim.x * blockDim.x;
   const bool vec = (p.N % 4) == 0;
   const bool rows_fast = p.c_ms == 1 && p.c_ns != 1;
-  for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < total; i += stride) {
-    int64_t row;
-    int32_t quad;
-    if (rows_fast) {
+  const int g = threadIdx.x % kReduceChunks;
+  const int32_t run = (p.splits + kReduceChunks - 1) / kReduceChunks;
+  const int32_t s_begin = min(p.splits, g * run), s_end = min(p.splits, s_begin + run);
+  // the loop bound is block-uniform, so every lane reaches the shuffles of every pass
+  for (int64_t i0 = (int64_t)blockIdx.x * kQuadsPerBlock; i0 < total; i0 += (int64_t)gridDim.x * kQuadsPerBlock) {
+    const int64_t i = i0 + threadIdx.x / kReduceChunks;
+    const bool active = i < total;
+    int64_t row = 0;
+    int32_t quad = 0;
+    if (!active) {
+    } else if (rows_fast) {
       const int64_t bq = i / p.M;  // (batch, quad) pair
       const int32_t m = (int32_t)(i - bq * p.M);
       const int64_t b = bq / nq;
@@ -1232,20 +1252,39 @@ __global__ void __launch_bounds__(256) splitk_reduce_kernel(const KParams p) {
       quad = (int32_t)(i - row * nq);
     }
     const int32_t n0 = quad * 4;
-    const int32_t b = (int32_t)(row / p.M), m = (int32_t)(row - (int64_t)b * p.M);
     float acc[4] = {0.f, 0.f, 0.f, 0.f};
     const float* src = p.partial + row * p.N + n0;
-    for (int s = 0; s < p.splits; s++, src += plane) {
-      if (vec) {
-        const float4 v = __ldcs(reinterpret_cast<const float4*>(src));
-        acc[0] = __fadd_rn(acc[0], v.x);
-        acc[1] = __fadd_rn(acc[1], v.y);
-        acc[2] = __fadd_rn(acc[2], v.z);
-        acc[3] = __fadd_rn(acc[3], v.w);
-      } else {
-        for (int e = 0; e < 4 && n0 + e < p.N; e++) acc[e] = __fadd_rn(acc[e], src[e]);
+    if (active && vec) {
+#pragma unroll 1
+      for (int s0 = s_begin; s0 < s_end; s0 += kReduceDepth) {
+        float4 v[kReduceDepth];
+        const float* sp = src + (int64_t)s0 * plane;
+#pragma unroll
+        for (int u = 0; u < kReduceDepth; u++, sp += plane)
+          if (s0 + u < s_end) v[u] = __ldcs(reinterpret_cast<const float4*>(sp));
+#pragma unroll
+        for (int u = 0; u < kReduceDepth; u++) {
+          if (s0 + u < s_end) {
+            acc[0] = __fadd_rn(acc[0], v[u].x);
+            acc[1] = __fadd_rn(acc[1], v[u].y);
+            acc[2] = __fadd_rn(acc[2], v[u].z);
+            acc[3] = __fadd_rn(acc[3], v[u].w);
+          }
+        }
       }
+    } else if (active) {
+      for (int s = s_begin; s < s_end; s++)
+        for (int e = 0; e < 4 && n0 + e < p.N; e++) acc[e] = __fadd_rn(acc[e], src[(int64_t)s * plane + e]);
     }
+    // the runs' sums in run order from +0 (a run past the last split adds +0, which changes no
+    // sum that started from +0)
+    float tot[4] = {0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+    for (int j = 0; j < kReduceChunks; j++)
+#pragma unroll
+      for (int e = 0; e < 4; e++) tot[e] = __fadd_rn(tot[e], __shfl_sync(0xffffffffu, acc[e], j, kReduceChunks));
+    if (!active || g != 0) continue;
+    const int32_t b = (int32_t)(row / p.M), m = (int32_t)(row - (int64_t)b * p.M);
     const int64_t base = p.c_off + (int64_t)b * p.c_bs + (int64_t)m * p.c_ms;
     float old[4];
 #pragma unroll
@@ -1253,7 +1292,7 @@ __global__ void __launch_bounds__(256) splitk_reduce_kernel(const KParams p) {
       old[e] = n0 + e < p.N ? read_old<EPI>(p, base + (int64_t)(n0 + e) * p.c_ns) : 0.0f;
 #pragma unroll
     for (int e = 0; e < 4; e++)
-      if (n0 + e < p.N) write_new<EPI>(p, base + (int64_t)(n0 + e) * p.c_ns, acc[e], old[e]);
+      if (n0 + e < p.N) write_new<EPI>(p, base + (int64_t)(n0 + e) * p.c_ns, tot[e], old[e]);
   }
 }
 
@@ -1828,12 +1867,24 @@ lc_status gemm_run(lc_context* ctx, cudaStream_t s, const GemmProblem& pr, lc_co
   }
   if (st == LC_OK && splits > 1 && !pair && !p.fixup) {
     const int64_t quads = (int64_t)pr.batch * M * ((N + 3) / 4);
-    const int rgrid = (int)std::max<int64_t>(1, std::min<int64_t>(ceil_div(quads, 256), (int64_t)ctx->sm_count * 8));
-    if (pr.epi == 0) splitk_reduce_kernel<0><<<rgrid, 256, 0, s>>>(p);
-    else if (pr.epi == 1) splitk_reduce_kernel<1><<<rgrid, 256, 0, s>>>(p);
-    else splitk_reduce_kernel<2><<<rgrid, 256, 0, s>>>(p);
+    const int rgrid = (int)std::max<int64_t>(
+        1, std::min<int64_t>(ceil_div(quads, kReduceBlock / kReduceChunks), (int64_t)ctx->sm_count * 16));
+    // a programmatic dependent of the GEMM: its blocks are resident and waiting when the last
+    // partial lands (measured 62.1 -> 60.3 us on the 256 x 256 x 262144 bf16 product)
+    cudaLaunchConfig_t cfg{};
+    cfg.gridDim = dim3((unsigned)rgrid);
+    cfg.blockDim = dim3(kReduceBlock);
+    cfg.stream = s;
+    cudaLaunchAttribute at[1];
+    at[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    at[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = at;
+    cfg.numAttrs = 1;
+    cudaError_t e = pr.epi == 0   ? cudaLaunchKernelEx(&cfg, splitk_reduce_kernel<0>, p)
+                    : pr.epi == 1 ? cudaLaunchKernelEx(&cfg, splitk_reduce_kernel<1>, p)
+                                  : cudaLaunchKernelEx(&cfg, splitk_reduce_kernel<2>, p);
     record_launch(ctx, "gemm_splitk_reduce");
-    cudaError_t e = cudaGetLastError();
+    if (e == cudaSuccess) e = cudaGetLastError();
     if (e != cudaSuccess) st = cuda_fail(e, "split-K reduce launch");
   }
   if (scratch) scratch_free(scratch, s);

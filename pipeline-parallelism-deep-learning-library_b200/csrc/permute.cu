@@ -117,26 +117,57 @@ __global__ void __launch_bounds__(256) copy_scalar_kernel(const E* __restrict__ 
 // ---- rows ---------------------------------------------------------------------------------------
 // Work item = one word of one row.  Row r's outer offsets come from decoding r over the outer axes
 // (g.rank of them); the words of a row are contiguous on both sides.  src/dst are word pointers
-// already advanced by the byte offsets.
+// already advanced by the byte offsets.  Each thread moves kRowUnroll words per pass, all loads
+// before any store, so that several loads per thread are in flight (one at a time left the copy
+// latency-bound).
+constexpr int kRowUnroll = 4;
+
+// Streaming row load.  16-byte words carry an L2 fetch-size hint of 64 bytes: a sliced row that
+// covers half of each of two 128-byte lines (32 floats from byte 64 of a 256-byte row) otherwise
+// pulls both whole lines from DRAM, twice the bytes the copy uses.
+template <typename Wd>
+__device__ __forceinline__ Wd ld_row_word(const Wd* p) {
+  if constexpr (sizeof(Wd) == 16) {
+    uint4 v;
+    asm volatile("ld.global.cs.L2::64B.v4.u32 {%0, %1, %2, %3}, [%4];"
+                 : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w)
+                 : "l"(p));
+    return *reinterpret_cast<Wd*>(&v);
+  } else {
+    return __ldcs(p);
+  }
+}
+
 template <typename Wd, bool SMALL>
 __global__ void __launch_bounds__(256) copy_rows_kernel(const Wd* __restrict__ src, Wd* __restrict__ dst, Geom g) {
   const uint64_t stride = (uint64_t)gridDim.x * blockDim.x;
-  for (uint64_t i = blockIdx.x * (uint64_t)blockDim.x + threadIdx.x; i < g.count; i += stride) {
-    uint64_t row, col;
-    if (g.words_shift != 0xffffffffu) {
-      row = i >> g.words_shift;
-      col = i & (g.row_words - 1);
-    } else if (SMALL) {
-      uint32_t q = fdiv((uint32_t)i, g.row_div);
-      row = q;
-      col = (uint32_t)i - q * g.row_div.d;
-    } else {
-      row = i / g.row_words;
-      col = i - row * g.row_words;
+  for (uint64_t i0 = blockIdx.x * (uint64_t)blockDim.x + threadIdx.x; i0 < g.count; i0 += stride * kRowUnroll) {
+    Wd v[kRowUnroll];
+    uint64_t at[kRowUnroll];
+#pragma unroll
+    for (int u = 0; u < kRowUnroll; u++) {
+      const uint64_t i = i0 + u * stride;
+      if (i >= g.count) continue;
+      uint64_t row, col;
+      if (g.words_shift != 0xffffffffu) {
+        row = i >> g.words_shift;
+        col = i & (g.row_words - 1);
+      } else if (SMALL) {
+        uint32_t q = fdiv((uint32_t)i, g.row_div);
+        row = q;
+        col = (uint32_t)i - q * g.row_div.d;
+      } else {
+        row = i / g.row_words;
+        col = i - row * g.row_words;
+      }
+      uint64_t so, dof;
+      decode<SMALL>(g, row, &so, &dof);
+      v[u] = ld_row_word(src + so + col);
+      at[u] = dof + col;
     }
-    uint64_t so, dof;
-    decode<SMALL>(g, row, &so, &dof);
-    dst[dof + col] = conj_word(__ldcs(src + so + col), g.conj);
+#pragma unroll
+    for (int u = 0; u < kRowUnroll; u++)
+      if (i0 + u * stride < g.count) dst[at[u]] = conj_word(v[u], g.conj);
   }
 }
 

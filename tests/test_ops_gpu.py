@@ -269,6 +269,41 @@ def test_argmax_rows_wide_and_misaligned(ctx, rows, cols, offset):
     assert (out.cpu().numpy() == want).all(), (out.cpu().numpy(), want)
 
 
+@pytest.mark.parametrize("cols", [16, 32, 64, 128, 256, 512])
+@pytest.mark.parametrize("rows", [1, 257, 3001])
+def test_argmax_rows_power_of_two_widths(ctx, rows, cols):
+    """The lane-scanning kernel for 16..512-float rows: each lane holds 16 values at columns
+    4 * (lane + L * j) + e, so ties inside one lane, ties across lanes, NaN after and before an
+    infinity, negative zero against zero, and a row count that leaves a partial pass must all
+    give the reference's lowest-index-wins result."""
+    x = data.normal(rows * 7 + cols, (rows, cols))
+    specials = SPECIALS.view(np.float32)
+    rng = np.random.default_rng(rows + cols)
+    for r in range(0, rows, 3):              # rows with special values at random columns
+        at = rng.choice(cols, size=min(6, cols), replace=False)
+        x[r, at] = specials[rng.integers(0, len(specials), size=len(at))]
+    x[0, :] = 0.0
+    x[0, cols // 2] = -0.0                   # -0 ties +0: index 0
+    if rows > 1:
+        x[1, :] = 2.0
+        x[1, 1] = -2.0                       # all tied: index 0
+    if rows > 2:
+        x[2, cols - 1] = np.nan
+        x[2, 3] = np.inf                     # NaN outranks inf wherever it sits
+    if rows > 3:
+        x[3, 4 * (cols // 16) + 2] = 9.0     # one lane's second float4 against
+        x[3, 2] = -9.0                       # the first lane's: the lower column wins
+    if rows > 4:
+        x[4, :] = np.nan                     # NaNs of several payloads after an infinity:
+        x[4, 0] = -np.inf                    # the first NaN, index 1
+        x[4, 1] = np.uint32(0x7fc00001).view(np.float32)
+    t = dev(x)
+    out = torch.empty((rows,), dtype=torch.uint32, device="cuda")
+    lb.argmax_rows(ctx, t, out)
+    want = O.argmax_rows(x)
+    assert (out.cpu().numpy() == want).all(), np.nonzero(out.cpu().numpy() != want)[0][:10]
+
+
 # ------------------------------------------------------------------------------------------------
 # contraction
 # ------------------------------------------------------------------------------------------------
