@@ -64,6 +64,13 @@ struct KParams {
   const void* aux;
   void* aux2;
   float lr;
+  // 3xTF32: a unit whose operand tiles hold an infinity or NaN is recomputed exactly on the CUDA
+  // cores from the operands as plain f32 arrays (element offsets applied): A (rows M) element
+  // [b * fa_bs + m * fa_ms + k * fa_ks], B (rows N) element [b * fb_bs + n * fb_ns + k * fb_ks]
+  const float* fa;
+  const float* fb;
+  int64_t fa_ms, fa_ks, fa_bs, fb_ns, fb_ks, fb_bs;
+  int64_t K;
 };
 
 constexpr int kSmemMax = 232448;  // dynamic shared memory a CTA may opt in to on sm_100
@@ -87,12 +94,15 @@ struct Cfg {
   static constexpr int TMEM_COLS = TMEM_NEED <= 32 ? 32 : TMEM_NEED <= 64 ? 64 : TMEM_NEED <= 128 ? 128
                                    : TMEM_NEED <= 256 ? 256 : 512;
   static_assert(TMEM_NEED <= 512, "TMEM holds 512 columns");
-  static constexpr int THREADS = TF32X3 ? 320 : 192;
+  // 3xTF32: 8 converter warps (two per SM sub-partition) hide the shared-memory latency that
+  // one warp per sub-partition left exposed
+  static constexpr int CONV_THREADS = TF32X3 ? 256 : 0;
+  static constexpr int THREADS = 192 + CONV_THREADS;
   // k-tiles per accumulator hand-off: one per unit for 16-bit inputs; 2 (64 K values, 24 MMAs)
   // for 3xTF32, which bounds the truncation bias of the tensor core's f32 accumulation to
   // about 24 ulp-halves per chunk while the chunks themselves are summed round-to-nearest.
   static constexpr int KC = TF32X3 ? 2 : (1 << 30);
-  static constexpr int BAR_BYTES = 8 * (3 * STAGES + 7) + 16;
+  static constexpr int BAR_BYTES = 8 * (3 * STAGES + 7) + 16 + 32;  // + 8 non-finite unit stamps
   // non-pair kernels: one 32 x 36 f32 tile per epilogue warp for coalesced row stores
   static constexpr int EPI_STAGE_BYTES = PAIR ? 0 : 4 * 32 * 36 * 4;
   static constexpr int SMEM = STAGES * STAGE_BYTES + ((BAR_BYTES + 15) / 16) * 16 + RECV_BYTES + EPI_STAGE_BYTES + 1024;
@@ -522,6 +532,25 @@ __device__ __forceinline__ void sum_partials(const KParams& p, float (&v)[32], i
   }
 }
 
+// 32 columns [n0, n0 + 32) of row m of one batch's product over K values [k0, k1), summed in k
+// order from +0 with separately rounded products (IEEE infinities and NaNs as the CPU backend
+// gives them), written to out[0..31]: the 3xTF32 path's fallback for units whose operands are
+// not all finite.  One column at a time, so it holds few registers in the epilogue warps.
+__device__ __noinline__ void exact_f32_row(const float* fa, const float* fb, int64_t fa_ms, int64_t fa_ks,
+                                           int64_t fa_bs, int64_t fb_ns, int64_t fb_ks, int64_t fb_bs, int32_t M,
+                                           int32_t N, int32_t b, int32_t m, int32_t n0, int64_t k0, int64_t k1,
+                                           float* out) {
+  const float* arow = fa + (int64_t)b * fa_bs + (int64_t)m * fa_ms;
+  for (int j = 0; j < 32; j++) {
+    float acc = 0.0f;
+    if (m < M && n0 + j < N) {
+      const float* bcol = fb + (int64_t)b * fb_bs + (int64_t)(n0 + j) * fb_ns;
+      for (int64_t k = k0; k < k1; k++) acc = __fadd_rn(acc, __fmul_rn(arow[k * fa_ks], bcol[k * fb_ks]));
+    }
+    out[j] = acc;
+  }
+}
+
 // ---- where a kernel's products come from ------------------------------------------------------
 // OneProduct: the tensor maps and parameters of a single product, passed as kernel arguments.
 // ChainParams/ChainSrc: a chain of dependent products in one launch (product l + 1 reads what
@@ -612,6 +641,9 @@ __device__ __forceinline__ void gemm_body(const Src& src) {
   uint64_t* recv_free = drain + 2;  // PAIR: the peer has consumed what this CTA sent it (128 arrivals)
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain + 3);
   uint32_t* layer_done = tmem_slot + 1;  // chain: epilogue warps done with their products so far
+  // 3xTF32: stamp uo + 1 in slot uo & 7 when the converters of this CTA's unit ordinal uo meet an
+  // infinity or NaN (the converters run at most a few units ahead of the epilogue)
+  uint32_t* nonfinite = layer_done + 1;
   float* recv = reinterpret_cast<float*>(reinterpret_cast<uint8_t*>(bars) + ((C::BAR_BYTES + 15) / 16) * 16);
   float* epi_stage = recv + C::RECV_BYTES / 4;  // non-pair kernels: 4 x (32 x 36) f32
 
@@ -622,7 +654,7 @@ __device__ __forceinline__ void gemm_body(const Src& src) {
     for (int s = 0; s < C::STAGES; s++) {
       lcd::mbar_init(&full[s], 1);
       lcd::mbar_init(&empty[s], 1);
-      lcd::mbar_init(&conv[s], 128);
+      lcd::mbar_init(&conv[s], C::CONV_THREADS);
     }
     for (int a = 0; a < 2; a++) {
       lcd::mbar_init(&tfull[a], 1);
@@ -632,6 +664,7 @@ __device__ __forceinline__ void gemm_body(const Src& src) {
     lcd::mbar_init(recv_full, 128);
     lcd::mbar_init(recv_free, 128);
     *layer_done = 0;
+    for (int i = 0; i < 8; i++) nonfinite[i] = 0;
     lcd::fence_mbar_init();
   }
   if (warp == 1) {
@@ -878,11 +911,12 @@ __device__ __forceinline__ void gemm_body(const Src& src) {
     const uint32_t lane_base = tmem_base + ((uint32_t)(q * 32) << 16);
     int32_t h = 0;
     bool ok = true;
+    uint32_t uo = 0;  // unit ordinal (the converters count the same units)
     lcd::griddep_wait();
     for (int l = 0; ok && l < src.layers(); l++) {
     decltype(auto) p = src.kp(l);  // a chain's are copied to registers once per product
     const bool split_mode = p.splits > 1 && !PAIR;
-    for (int32_t u = u_first; ok && u < p.units; u += u_step) {
+    for (int32_t u = u_first; ok && u < p.units; u += u_step, uo++) {
       int32_t b, split, tm, tn;
       unit_coords(p, u, &b, &split, &tm, &tn);
       const int32_t m = tile_row0(tm) + q * 32 + lane;
@@ -944,11 +978,23 @@ __device__ __forceinline__ void gemm_body(const Src& src) {
           lcd::mbar_arrive(&tempty[acc]);
         }
         if (!ok) break;
+        // every conversion of this unit preceded its last hand-off, so its stamp is in place
+        const bool exact = *reinterpret_cast<volatile uint32_t*>(&nonfinite[uo & 7]) == uo + 1;
 #pragma unroll 1
         for (int g = 0; g < BN / 32; g++) {
           uint32_t r[32];
-          lcd::tmem_ld_32x32b_x32(run_base + g * 32, r);
-          lcd::tmem_ld_wait();
+          if (!exact) {
+            lcd::tmem_ld_32x32b_x32(run_base + g * 32, r);
+            lcd::tmem_ld_wait();
+          } else {
+            // through this warp's staging tile (row = lane), read back before emit reuses it
+            float* row = epi_stage + (warp - 2) * (32 * 36) + lane * 36;
+            exact_f32_row(p.fa, p.fb, p.fa_ms, p.fa_ks, p.fa_bs, p.fb_ns, p.fb_ks, p.fb_bs, p.M, p.N, b, m,
+                          tn * BN + g * 32, (int64_t)kb * C::BK, min((int64_t)ke * C::BK, p.K), row);
+#pragma unroll
+            for (int j = 0; j < 32; j++) r[j] = __float_as_uint(row[j]);
+            __syncwarp();
+          }
           emit(r, tn * BN + g * 32);
         }
       } else if constexpr (PAIR) {
@@ -1116,13 +1162,21 @@ __device__ __forceinline__ void gemm_body(const Src& src) {
     }
   } else if constexpr (TF32X3) {
     // ---------------- 3xTF32 split ----------------
-    const int ct = threadIdx.x - 192;  // 0..127
+    // The tensor core reads a 32-bit operand as tf32 by ignoring its low 13 mantissa bits
+    // (truncation: the f32 accuracy tests, 1e-5 normwise, would fail by an order of magnitude
+    // if it rounded), so the raw f32 the TMA put in the stage serves unchanged as hi =
+    // trunc(x).  lo = x - hi is exact in f32; it is rounded to tf32 here (nearest, ties away)
+    // into the stage's lo half, so the tensor core reads it exactly.  Three products cannot
+    // carry IEEE infinities (inf * hi(b) + inf * lo(b) is NaN when lo(b) = 0), so an infinite
+    // or NaN x only marks the unit, whose epilogue then recomputes the tile exactly.
+    const int ct = threadIdx.x - 192;  // 0 .. CONV_THREADS - 1
     int s = 0;
     uint32_t ph = 0;
     bool ok = true;
+    uint32_t uo = 0;  // unit ordinal
     for (int l = 0; ok && l < src.layers(); l++) {
     decltype(auto) p = src.kp(l);  // a chain's are copied to registers once per product
-    for (int32_t u = blockIdx.x; ok && u < p.units; u += gridDim.x) {
+    for (int32_t u = blockIdx.x; ok && u < p.units; u += gridDim.x, uo++) {
       int32_t b, split, tm, tn;
       unit_coords(p, u, &b, &split, &tm, &tn);
       const int32_t kb = split * p.kt_per_split;
@@ -1133,30 +1187,34 @@ __device__ __forceinline__ void gemm_body(const Src& src) {
           break;
         }
         // elementwise on identical layouts, so the swizzle is irrelevant
-        uint4* hi = reinterpret_cast<uint4*>(a_hi(s));
+        const uint4* raw = reinterpret_cast<const uint4*>(a_hi(s));
         uint4* lo = reinterpret_cast<uint4*>(a_lo(s));
         constexpr int NV = (C::A_BYTES + C::B_BYTES) / 16;
-        for (int v = ct; v < NV; v += 128) {
-          uint4 x = hi[v];
-          uint4 h, l;
-          const uint32_t* xs = reinterpret_cast<const uint32_t*>(&x);
-          uint32_t* hs = reinterpret_cast<uint32_t*>(&h);
-          uint32_t* ls = reinterpret_cast<uint32_t*>(&l);
+        constexpr int CT = C::CONV_THREADS;
+        static_assert(NV % (CT * 2) == 0, "converter passes of 2 vectors per thread");
+#pragma unroll 1
+        for (int v0 = ct; v0 < NV; v0 += CT * 2) {
+          uint4 x[2];
 #pragma unroll
-          for (int e = 0; e < 4; e++) {
-            // hi = x rounded to tf32 (11 significant bits, nearest, ties away); lo = x - hi is
-            // exact in f32 and is itself rounded to tf32 the same way, so the tensor core reads
-            // both exactly whatever its own conversion does.
-            uint32_t hb = (xs[e] + 0x1000u) & 0xffffe000u;
-            if (((hb >> 23) & 0xffu) == 0xffu && ((xs[e] >> 23) & 0xffu) != 0xffu) hb = xs[e] & 0xffffe000u;
-            const float hf = __uint_as_float(hb);
-            hs[e] = hb;
-            // an infinite or NaN hi carries the value alone (its lo would be NaN)
-            const uint32_t lb = __float_as_uint(__fsub_rn(__uint_as_float(xs[e]), hf));
-            ls[e] = isfinite(hf) ? ((lb + 0x1000u) & 0xffffe000u) : 0u;
+          for (int q = 0; q < 2; q++) x[q] = raw[v0 + CT * q];
+#pragma unroll
+          for (int q = 0; q < 2; q++) {
+            uint4 lv;
+            const uint32_t* xs = reinterpret_cast<const uint32_t*>(&x[q]);
+            uint32_t* ls = reinterpret_cast<uint32_t*>(&lv);
+            uint32_t big = 0;
+#pragma unroll
+            for (int e = 0; e < 4; e++) {
+              const float d = __fsub_rn(__uint_as_float(xs[e]), __uint_as_float(xs[e] & 0xffffe000u));
+              ls[e] = (__float_as_uint(d) + 0x1000u) & 0xffffe000u;
+              big = max(big, xs[e] & 0x7fffffffu);
+            }
+            if (big >= 0x7f800000u) {
+              nonfinite[uo & 7] = uo + 1;
+              __threadfence_block();
+            }
+            lo[v0 + CT * q] = lv;
           }
-          hi[v] = h;
-          lo[v] = l;
         }
         lcd::fence_proxy_async_smem();
         lcd::mbar_arrive(&conv[s]);
@@ -1732,6 +1790,17 @@ lc_status plan_gemm(lc_context* ctx, const lc::GemmProblem& pr, lc_contract_plan
   p.alpha = pr.alpha;
   p.beta = pr.beta;
   p.err = ctx->d_error;
+  if (tf32x3) {
+    p.fa = static_cast<const float*>(A.data) + A.offset;
+    p.fb = static_cast<const float*>(B.data) + B.offset;
+    p.fa_ms = A.mn_stride;
+    p.fa_ks = A.k_stride;
+    p.fa_bs = A.batch > 1 ? A.batch_stride : 0;
+    p.fb_ns = B.mn_stride;
+    p.fb_ks = B.k_stride;
+    p.fb_bs = B.batch > 1 ? B.batch_stride : 0;
+    p.K = (int64_t)pr.k;
+  }
   if (tf32x3 && pr.epi != 0) return fail(LC_ERR_INVALID_ARGUMENT, "fused epilogues take 16-bit inputs");
   if (pr.epi < 0 || pr.epi > 2) return fail(LC_ERR_INVALID_ARGUMENT, "unknown epilogue");
   {

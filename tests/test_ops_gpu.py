@@ -470,6 +470,39 @@ def test_contract_split_k_tall_bf16(ctx):
     assert rel <= BF16_TOL, rel
 
 
+@pytest.mark.parametrize("dtype", [torch.float32, torch.bfloat16, torch.float16])
+def test_contract_non_finite_inputs(ctx, dtype):
+    """NaN and infinity reach exactly the outputs that depend on them, including through ragged
+    boundary tiles and split-K (tests/contraction_test.rs:696-731): a NaN at A[m-1, k-1] and +inf
+    at B[k/2, n-2].  The 3xTF32 path recomputes such units exactly; the other outputs keep the
+    normwise tolerance against the f64 product of the finite inputs."""
+    for seed, (m, n, k) in enumerate([(70, 45, 50), (3, 2, 40_000), (9, 11, 1), (300, 200, 4096)]):
+        a = data.uniform(1400 + seed, (m, k))
+        b = data.uniform(1450 + seed, (k, n))
+        nan_row, inf_col = m - 1, n - 2
+        a[nan_row, k - 1] = np.nan
+        b[k // 2, inf_col] = np.inf
+        ta, tb = dev(a).to(dtype), dev(b).to(dtype)
+        c = torch.zeros((m, n), dtype=dtype, device="cuda")
+        lb.contract(ctx, 1.0, (ta, "ik"), (tb, "kj"), 0.0, (c, "ij"))
+        got = to_np_f32(c).astype(np.float64)
+        an, bn = to_np_f32(ta).astype(np.float64), to_np_f32(tb).astype(np.float64)
+        poisoned = np.zeros((m, n), bool)
+        poisoned[nan_row, :] = True
+        poisoned[:, inf_col] = True
+        assert (np.isfinite(got) == ~poisoned).all(), np.argwhere(np.isfinite(got) == poisoned)[:5]
+        assert np.isnan(got[nan_row, :]).all()
+        rows = np.arange(m) != nan_row
+        # an infinity times a nonzero finite a gives an infinity with a's sign (a is never 0 here)
+        assert (got[rows, inf_col] == np.inf * np.sign(an[rows, k // 2])).all()
+        af, bf = np.where(np.isfinite(an), an, 0.0), np.where(np.isfinite(bn), bn, 0.0)
+        exact = af @ bf
+        keep = ~poisoned
+        denom = max(np.abs(exact[keep]).max(), 1e-30)
+        rel = np.abs(got[keep] - exact[keep]).max() / denom
+        assert rel <= (F32_TOL if dtype == torch.float32 else BF16_TOL), (m, n, k, rel)
+
+
 def test_contract_determinism(ctx):
     a = dev(data.uniform(1300, (4, 300_000)))
     b = dev(data.uniform(1301, (300_000, 4)))
