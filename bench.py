@@ -299,6 +299,34 @@ def run_profile(args):
         ctx.sync()
         print(json.dumps({"profile": "gemm", "launches": ctx.debug_launches()[-8:]}))
         return 0
+    if args.profile == "ops":
+        # one round = slice+pack, bf16 split-K, f32 split-K (3xTF32), argmax over the last axis,
+        # permute (0,3,1,2), sqrt: the configs of the op figures, in that launch order
+        ctx = lb.Context(0)
+        st = ctx.stream
+        x = torch.randn(64, 128, 128, 64, device="cuda")
+        sl = lb.slice(x, [range(0, 64), range(32, 96), range(0, 128), range(16, 48)])
+        packed = torch.empty(sl.shape, device="cuda")
+        K = 262144
+        a = torch.randn(256, K, device="cuda") / K ** 0.5
+        b = torch.randn(K, 256, device="cuda") / K ** 0.5
+        c = torch.empty(256, 256, device="cuda")
+        ab, bb, cb = a.bfloat16(), b.bfloat16(), c.bfloat16()
+        am = torch.empty(64, 128, 128, dtype=torch.uint32, device="cuda")
+        perm = lb.permute_view(x, [0, 3, 1, 2])
+        permuted = torch.empty(perm.shape, device="cuda")
+        xp = x.abs() + 1e-3
+        y = torch.empty_like(x)
+        for _ in range(args.warmup + args.steps):
+            lb.encode_pack(ctx, st, sl, packed)
+            lb.encode_contract(ctx, st, 1.0, (ab, "ik"), (bb, "kj"), 0.0, (cb, "ij"))
+            lb.encode_contract(ctx, st, 1.0, (a, "ik"), (b, "kj"), 0.0, (c, "ij"))
+            lb.encode_argmax_rows(ctx, st, x, am)
+            lb.encode_materialize(ctx, st, perm, permuted)
+            lb.encode_sqrt(ctx, st, xp, y)
+        ctx.sync()
+        print(json.dumps({"profile": "ops", "launches": ctx.debug_launches()[-9:]}))
+        return 0
     p = Pipeline(args.layers, WIDTH, MB, MBS, lr=LR)
     p.init_weights(1234, WIDTH ** -0.5)
     x = torch.from_numpy(data.normal(1, (BATCH, WIDTH))).cuda()
@@ -321,9 +349,11 @@ def main():
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--no-extras", action="store_true", help="skip the N=1 contraction/op figures")
     ap.add_argument("--layers", type=int, default=LAYERS, help="profiling driver only: pipeline depth")
-    ap.add_argument("--profile", choices=["step", "gemm"], default=None,
+    ap.add_argument("--profile", choices=["step", "gemm", "ops"], default=None,
                     help="profiling driver: 'step' runs --warmup + --steps pipeline steps and nothing else; "
-                         "'gemm' runs --steps forward-shaped GEMMs ([64,8192] x [8192,8192] bf16)")
+                         "'gemm' runs --steps forward-shaped GEMMs ([64,8192] x [8192,8192] bf16); "
+                         "'ops' runs --warmup + --steps rounds of the op-figure configs (pack, bf16 and "
+                         "f32 split-K, argmax rows, permute, sqrt)")
     args = ap.parse_args()
     if args.impl == "reference":
         return run_reference(args)
