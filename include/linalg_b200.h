@@ -191,7 +191,9 @@ lc_status lc_encode_argmax_complex(lc_context* ctx, void* stream, const lc_view*
 /* Correctly rounded sqrt: bitwise (x as f64).sqrt() as f32.  In place when src == dst. */
 lc_status lc_encode_sqrt(lc_context* ctx, void* stream, const lc_view* src, const lc_view* dst);
 lc_status lc_sqrt(lc_context* ctx, const lc_view* src, const lc_view* dst);
-/* Correctly rounded 1/x: bitwise (1.0 / x as f64) as f32 (real f32 only). */
+/* 1/x.  Real f32: correctly rounded, bitwise (1.0 / x as f64) as f32.  Complex f32 (LC_C32):
+ * Smith's algorithm on split floats with the C99 Annex G specials, bit for bit as the
+ * reference kernel (src/ops/reciprocal.rs:17-31, shaders/reciprocal.metal:141-330). */
 lc_status lc_encode_reciprocal(lc_context* ctx, void* stream, const lc_view* src, const lc_view* dst);
 lc_status lc_reciprocal(lc_context* ctx, const lc_view* src, const lc_view* dst);
 

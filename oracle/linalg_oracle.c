@@ -330,6 +330,132 @@ void or_reciprocal(const float* x, float* y, uint64_t n) {
 }
 
 /* ------------------------------------------------------------------------------------ */
+/* Complex reciprocal: src/ops/reciprocal.rs:17-31 (documented rules) and                 */
+/* shaders/reciprocal.metal:141-330 (the algorithm).  Smith's method on "split" floats:   */
+/* a value is a significand m with |m| in [1, 2) (or a signed zero) and an exponent e,    */
+/* x = m * 2^e, so no intermediate overflows, underflows or is flushed; every product and */
+/* sum of significands is one f32 rounding, every division is the correctly rounded real */
+/* reciprocal times the dividend, and the result is packed into f32 once (a subnormal    */
+/* result rounds the 24-bit significand right, nearest even).                            */
+/* ------------------------------------------------------------------------------------ */
+typedef struct { float m; int e; } split_f;
+
+static inline float rcp_cr(float x) { return (float)(1.0 / (double)x); }
+
+/* nonzero finite bits -> split float (:141-153) */
+static split_f split_of(uint32_t bits) {
+    uint32_t ex = (bits >> 23) & 0xffu, fr = bits & 0x007fffffu, sg = bits & 0x80000000u;
+    split_f s;
+    if (ex == 0u) {
+        int lead = 0;                      /* leading zeros of the 23-bit fraction in 32 bits */
+        while (lead < 32 && !(fr & (0x80000000u >> lead))) lead++;
+        int sh = lead - 8;
+        s.m = u2f(((fr << sh) & 0x007fffffu) | (127u << 23) | sg);
+        s.e = -126 - sh;
+    } else {
+        s.m = u2f((bits & 0x807fffffu) | (127u << 23));
+        s.e = (int)ex - 127;
+    }
+    return s;
+}
+
+static split_f split_mul(split_f a, split_f b) {           /* :207-218 */
+    split_f r;
+    if (a.m == 0.0f || b.m == 0.0f) { r.m = a.m * b.m; r.e = 0; return r; }
+    float p = a.m * b.m;
+    if (fabsf(p) >= 2.0f) { r.m = p * 0.5f; r.e = a.e + b.e + 1; }
+    else { r.m = p; r.e = a.e + b.e; }
+    return r;
+}
+
+static split_f split_rcp(split_f a) {                      /* :220-227 */
+    split_f r;
+    float inv = rcp_cr(a.m);
+    if (fabsf(inv) < 1.0f) { r.m = inv * 2.0f; r.e = -a.e - 1; }
+    else { r.m = inv; r.e = -a.e; }
+    return r;
+}
+
+static split_f split_add_same_sign(split_f a, split_f b) { /* :233-256 */
+    if (b.m == 0.0f) return a;
+    if (a.m == 0.0f) return b;
+    if (a.e < b.e) { split_f t = a; a = b; b = t; }
+    int diff = a.e - b.e;
+    if (diff >= 25) return a;
+    float s = a.m + b.m * u2f((uint32_t)(127 - diff) << 23);
+    split_f r;
+    if (fabsf(s) >= 2.0f) { r.m = s * 0.5f; r.e = a.e + 1; }
+    else { r.m = s; r.e = a.e; }
+    return r;
+}
+
+static int split_abs_ge(split_f a, split_f b) {            /* :258-271 */
+    int az = a.m == 0.0f, bz = b.m == 0.0f;
+    if (az) return bz;
+    if (bz) return 1;
+    if (a.e != b.e) return a.e > b.e;
+    return fabsf(a.m) >= fabsf(b.m);
+}
+
+static uint32_t split_bits(split_f s) {                    /* :171-201 */
+    uint32_t raw = f2u(s.m), sign = raw & 0x80000000u;
+    if ((raw & 0x7fffffffu) == 0u) return sign;
+    if (s.e >= 128) return sign | 0x7f800000u;
+    if (s.e >= -126) return (raw & 0x807fffffu) | ((uint32_t)(s.e + 127) << 23);
+    uint32_t rshift = (uint32_t)(-s.e - 126);
+    uint32_t mant = (raw & 0x007fffffu) | 0x00800000u;
+    uint32_t m;
+    if (rshift >= 25u) {
+        m = 0u;
+    } else {
+        uint32_t kept = mant >> rshift, rem = mant & ((1u << rshift) - 1u), half = 1u << (rshift - 1u);
+        m = (rem > half || (rem == half && (kept & 1u))) ? kept + 1u : kept;
+    }
+    if (m == 0u) return sign;
+    return sign | m;  /* m <= 2^23: a subnormal, or the carry into the smallest normal */
+}
+
+static split_f split_neg(split_f a) { a.m = -a.m; return a; }
+
+/* :285-330 */
+void or_reciprocal_c32(const uint32_t* z, uint32_t* w, uint64_t n) {
+    for (uint64_t i = 0; i < n; i++) {
+        uint32_t ab = z[2 * i], bb = z[2 * i + 1];
+        uint32_t ae = (ab >> 23) & 0xffu, be = (bb >> 23) & 0xffu;
+        int a_inf = ae == 0xffu && !(ab & 0x007fffffu), b_inf = be == 0xffu && !(bb & 0x007fffffu);
+        int a_nan = ae == 0xffu && (ab & 0x007fffffu), b_nan = be == 0xffu && (bb & 0x007fffffu);
+        uint32_t re, im;
+        if (a_inf || b_inf) {
+            re = ab & 0x80000000u;
+            im = (bb ^ 0x80000000u) & 0x80000000u;
+        } else if (a_nan || b_nan) {
+            re = im = 0x7fc00000u;
+        } else if (!(bb & 0x7fffffffu)) {
+            re = f2u(rcp_cr(u2f(ab)));
+            im = (bb ^ 0x80000000u) & 0x80000000u;
+        } else if (!(ab & 0x7fffffffu)) {
+            re = ab & 0x80000000u;
+            im = f2u(rcp_cr(u2f(bb))) ^ 0x80000000u;
+        } else {
+            split_f sa = split_of(ab), sb = split_of(bb);
+            if (split_abs_ge(sa, sb)) {
+                split_f r = split_mul(sb, split_rcp(sa));
+                split_f inv = split_rcp(split_add_same_sign(sa, split_mul(sb, r)));
+                re = split_bits(inv);
+                im = split_bits(split_mul(split_neg(r), inv));
+            } else {
+                split_f r = split_mul(sa, split_rcp(sb));
+                split_f inv = split_rcp(split_add_same_sign(sb, split_mul(sa, r)));
+                re = split_bits(split_mul(r, inv));
+                im = split_bits(split_neg(inv));
+            }
+        }
+        w[2 * i] = re;
+        w[2 * i + 1] = im;
+    }
+}
+
+/* ------------------------------------------------------------------------------------ */
 /* Training ops: crates/cpu/src/lib.rs:372-533 (sequential f32, no FMA).                  */
 /* ------------------------------------------------------------------------------------ */
 

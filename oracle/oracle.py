@@ -61,6 +61,7 @@ def lib() -> C.CDLL:
             "or_argmax_rows": (None, [_ptr, _u64, _u64, _u64, _u64, _ptr]),
             "or_sqrt": (None, [_ptr, _ptr, _u64]),
             "or_reciprocal": (None, [_ptr, _ptr, _u64]),
+            "or_reciprocal_c32": (None, [_ptr, _ptr, _u64]),
             "or_add_bias": (None, [_ptr, _ptr, _ptr, _u64, _u64]),
             "or_bias_grad": (None, [_ptr, _ptr, _u64, _u64]),
             "or_mse_grad": (_f32, [_ptr, _ptr, _ptr, _u64]),
@@ -287,6 +288,14 @@ def reciprocal(x: np.ndarray) -> np.ndarray:
     y = np.empty_like(x)
     lib().or_reciprocal(_p(x), _p(y), x.size)
     return y
+
+
+def reciprocal_c32(z: np.ndarray) -> np.ndarray:
+    """1/z for complex f32 (re, im) pairs, bit for bit as shaders/reciprocal.metal:285-330."""
+    z = np.ascontiguousarray(z, dtype=np.complex64)
+    w = np.empty_like(z)
+    lib().or_reciprocal_c32(_p(z), _p(w), z.size)
+    return w
 
 
 # ---------------------------------------------------------------------------------------------

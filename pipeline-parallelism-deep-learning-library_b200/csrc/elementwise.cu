@@ -134,6 +134,122 @@ __global__ void unary_strided_kernel(const float* src, float* dst, Strided p) {
   }
 }
 
+// ---- complex reciprocal (src/ops/reciprocal.rs:17-31, shaders/reciprocal.metal:141-330) -------
+// Smith's algorithm on split floats: a nonzero finite value is a significand m with |m| in
+// [1, 2) and an exponent e, x = m * 2^e, so no intermediate overflows, underflows or becomes
+// subnormal.  Each product or sum of significands is one IEEE f32 rounding, each division is
+// the dividend times the correctly rounded reciprocal of the divisor, and the parts are packed
+// into f32 once (a subnormal part rounds the 24-bit significand right, nearest even).  The
+// specials follow C99 Annex G as the reference documents them.
+struct Split {
+  float m;
+  int e;
+};
+
+// a nonzero finite f32 (subnormals normalised)
+__device__ __forceinline__ Split split_of(uint32_t b) {
+  const uint32_t ex = (b >> 23) & 0xffu, fr = b & 0x007fffffu, sg = b & 0x80000000u;
+  if (ex == 0u) {
+    const int sh = __clz((int)fr) - 8;
+    return {__uint_as_float(((fr << sh) & 0x007fffffu) | (127u << 23) | sg), -126 - sh};
+  }
+  return {__uint_as_float((b & 0x807fffffu) | (127u << 23)), (int)ex - 127};
+}
+
+__device__ __forceinline__ Split split_mul(Split a, Split b) {
+  if (a.m == 0.0f || b.m == 0.0f) return {__fmul_rn(a.m, b.m), 0};
+  const float p = __fmul_rn(a.m, b.m);
+  return fabsf(p) >= 2.0f ? Split{p * 0.5f, a.e + b.e + 1} : Split{p, a.e + b.e};
+}
+
+__device__ __forceinline__ Split split_rcp(Split a) {
+  const float inv = __frcp_rn(a.m);
+  return fabsf(inv) < 1.0f ? Split{inv * 2.0f, -a.e - 1} : Split{inv, -a.e};
+}
+
+// a + b for parts of one sign (Smith's denominator never cancels); b shifted by the exponent
+// gap, dropped from 25 binades down
+__device__ __forceinline__ Split split_add(Split a, Split b) {
+  if (b.m == 0.0f) return a;
+  if (a.m == 0.0f) return b;
+  if (a.e < b.e) {
+    const Split t = a;
+    a = b;
+    b = t;
+  }
+  const int gap = a.e - b.e;
+  if (gap >= 25) return a;
+  const float s = __fadd_rn(a.m, __fmul_rn(b.m, __uint_as_float((uint32_t)(127 - gap) << 23)));
+  return fabsf(s) >= 2.0f ? Split{s * 0.5f, a.e + 1} : Split{s, a.e};
+}
+
+__device__ __forceinline__ bool split_abs_ge(Split a, Split b) {
+  const bool az = a.m == 0.0f, bz = b.m == 0.0f;
+  if (az) return bz;
+  if (bz) return true;
+  if (a.e != b.e) return a.e > b.e;
+  return fabsf(a.m) >= fabsf(b.m);
+}
+
+__device__ __forceinline__ uint32_t split_bits(Split s) {
+  const uint32_t raw = __float_as_uint(s.m), sign = raw & 0x80000000u;
+  if ((raw & 0x7fffffffu) == 0u) return sign;
+  if (s.e >= 128) return sign | 0x7f800000u;
+  if (s.e >= -126) return (raw & 0x807fffffu) | ((uint32_t)(s.e + 127) << 23);
+  const uint32_t sh = (uint32_t)(-s.e - 126);
+  if (sh >= 25u) return sign;
+  const uint32_t mant = (raw & 0x007fffffu) | 0x00800000u;
+  const uint32_t kept = mant >> sh, rem = mant & ((1u << sh) - 1u), half = 1u << (sh - 1u);
+  // at most 2^23: a subnormal, or the carry into the smallest normal, which has these bits
+  return sign | ((rem > half || (rem == half && (kept & 1u))) ? kept + 1u : kept);
+}
+
+__device__ __forceinline__ uint2 rcp_c32(uint2 z) {
+  const uint32_t ab = z.x, bb = z.y;
+  const bool a_top = ((ab >> 23) & 0xffu) == 0xffu, b_top = ((bb >> 23) & 0xffu) == 0xffu;
+  const bool a_inf = a_top && !(ab & 0x007fffffu), b_inf = b_top && !(bb & 0x007fffffu);
+  if (a_inf || b_inf) return make_uint2(ab & 0x80000000u, ~bb & 0x80000000u);
+  if (a_top || b_top) return make_uint2(0x7fc00000u, 0x7fc00000u);  // a NaN part
+  if (!(bb & 0x7fffffffu)) return make_uint2(__float_as_uint(__frcp_rn(__uint_as_float(ab))), ~bb & 0x80000000u);
+  if (!(ab & 0x7fffffffu)) return make_uint2(ab & 0x80000000u, __float_as_uint(__frcp_rn(__uint_as_float(bb))) ^ 0x80000000u);
+  const Split a = split_of(ab), b = split_of(bb);
+  if (split_abs_ge(a, b)) {
+    const Split r = split_mul(b, split_rcp(a));                  // b / a
+    const Split inv = split_rcp(split_add(a, split_mul(b, r)));  // 1 / (a + b r)
+    return make_uint2(split_bits(inv), split_bits(split_mul(Split{-r.m, r.e}, inv)));
+  }
+  const Split r = split_mul(a, split_rcp(b));                    // a / b
+  const Split inv = split_rcp(split_add(b, split_mul(a, r)));    // 1 / (a r + b)
+  return make_uint2(split_bits(split_mul(r, inv)), split_bits(Split{-inv.m, inv.e}));
+}
+
+// One 16-byte vector (two complex values) per thread per pass.  (Four vectors in flight per
+// thread measured slower: the branchy special-case paths keep the compiler from interleaving
+// the values' dependent chains, and the extra registers cost occupancy.)
+__global__ void __launch_bounds__(256) rcp_c32_vec_kernel(const uint4* __restrict__ src, uint4* __restrict__ dst,
+                                                          uint64_t n2) {
+  const uint64_t stride = (uint64_t)gridDim.x * blockDim.x;
+  for (uint64_t i = blockIdx.x * (uint64_t)blockDim.x + threadIdx.x; i < n2; i += stride) {
+    const uint4 v = __ldcs(src + i);
+    const uint2 lo = rcp_c32(make_uint2(v.x, v.y)), hi = rcp_c32(make_uint2(v.z, v.w));
+    __stcs(dst + i, make_uint4(lo.x, lo.y, hi.x, hi.y));
+  }
+}
+
+__global__ void rcp_c32_scalar_kernel(const uint2* __restrict__ src, uint2* __restrict__ dst, uint64_t n) {
+  const uint64_t stride = (uint64_t)gridDim.x * blockDim.x;
+  for (uint64_t i = blockIdx.x * (uint64_t)blockDim.x + threadIdx.x; i < n; i += stride) dst[i] = rcp_c32(src[i]);
+}
+
+__global__ void rcp_c32_strided_kernel(const uint2* src, uint2* dst, Strided p) {
+  const uint64_t stride = (uint64_t)gridDim.x * blockDim.x;
+  for (uint64_t i = blockIdx.x * (uint64_t)blockDim.x + threadIdx.x; i < p.count; i += stride) {
+    uint64_t so, dof;
+    decode(p, i, &so, &dof);
+    dst[dof] = rcp_c32(src[so]);
+  }
+}
+
 unsigned grid_for(lc_context* ctx, uint64_t work, unsigned block) {
   uint64_t want = (work + block - 1) / block;
   uint64_t cap = (uint64_t)ctx->sm_count * 8;
@@ -153,8 +269,11 @@ lc_status run_unary(lc_context* ctx, void* stream, const lc_view* srcp, const lc
   lc_status st = validate(src, "src");
   if (st) return st;
   if ((st = validate(dst, "dst"))) return st;
-  if (src.dtype != LC_F32 || dst.dtype != LC_F32)
-    return fail(LC_ERR_INVALID_ARGUMENT, std::string(opname) + " supports real f32 views");
+  // sqrt: real f32; reciprocal: real f32 or complex [f32; 2] (src/ops/reciprocal.rs:49-61)
+  const bool complex = OP == 1 && src.dtype == LC_C32 && dst.dtype == LC_C32;
+  if (!complex && (src.dtype != LC_F32 || dst.dtype != LC_F32))
+    return fail(LC_ERR_INVALID_ARGUMENT, std::string(opname) + (OP == 1 ? " supports f32 and complex f32 views"
+                                                                        : " supports real f32 views"));
   if (src.rank != dst.rank || memcmp(src.shape, dst.shape, sizeof(uint64_t) * src.rank) != 0)
     return fail(LC_ERR_INVALID_ARGUMENT, std::string(opname) + " shape mismatch");
   bool inplace = same_view(src, dst);
@@ -165,9 +284,34 @@ lc_status run_unary(lc_context* ctx, void* stream, const lc_view* srcp, const lc
   if (!is_injective(dst))
     return fail(LC_ERR_INVALID_ARGUMENT, std::string(opname) + " destination is not injective; parallel stores would alias");
   cudaStream_t s = stream_of(ctx, stream);
+  uint64_t n = numel(src);
+  if (complex) {
+    const uint2* zp = static_cast<const uint2*>(src.data) + src.offset;
+    uint2* wp = static_cast<uint2*>(dst.data) + dst.offset;
+    if (is_contiguous(src) && is_contiguous(dst)) {
+      const bool aligned = (reinterpret_cast<uintptr_t>(zp) % 16 == 0) && (reinterpret_cast<uintptr_t>(wp) % 16 == 0);
+      const uint64_t n2 = aligned ? n / 2 : 0;
+      if (n2) {
+        rcp_c32_vec_kernel<<<grid_for(ctx, n2, 256), 256, 0, s>>>(reinterpret_cast<const uint4*>(zp),
+                                                                  reinterpret_cast<uint4*>(wp), n2);
+        record_launch(ctx, "reciprocal_c32_vec");
+      }
+      if (n - 2 * n2) {
+        rcp_c32_scalar_kernel<<<grid_for(ctx, n - 2 * n2, 256), 256, 0, s>>>(zp + 2 * n2, wp + 2 * n2, n - 2 * n2);
+        record_launch(ctx, "reciprocal_c32_scalar");
+      }
+    } else {
+      Strided p = merge_pair(src, dst);
+      rcp_c32_strided_kernel<<<grid_for(ctx, n, 256), 256, 0, s>>>(static_cast<const uint2*>(src.data),
+                                                                   static_cast<uint2*>(dst.data), p);
+      record_launch(ctx, "reciprocal_c32_strided");
+    }
+    cudaError_t e = cudaGetLastError();
+    if (e != cudaSuccess) return cuda_fail(e, opname);
+    return LC_OK;
+  }
   const float* sp = static_cast<const float*>(src.data) + src.offset;
   float* dp = static_cast<float*>(dst.data) + dst.offset;
-  uint64_t n = numel(src);
   if (is_contiguous(src) && is_contiguous(dst)) {
     bool aligned = (reinterpret_cast<uintptr_t>(sp) % 16 == 0) && (reinterpret_cast<uintptr_t>(dp) % 16 == 0);
     if (aligned && n >= 4) {

@@ -106,6 +106,89 @@ def test_elementwise_baseline_tensor_bit_exact(ctx, op):
 
 
 # ------------------------------------------------------------------------------------------------
+# complex reciprocal (src/ops/reciprocal.rs:17-31)
+# ------------------------------------------------------------------------------------------------
+
+def gpu_rcp_c32(ctx, z: np.ndarray) -> np.ndarray:
+    src = dev(np.ascontiguousarray(z, dtype=np.complex64))
+    dst = torch.empty_like(src)
+    lb.reciprocal(ctx, src, dst)
+    return dst.cpu().numpy()
+
+
+def test_complex_reciprocal_goldens(ctx):
+    """Every exact complex result the reference's tests assert (tests/reciprocal_test.rs:569-741),
+    bit for bit, and the NaN rule."""
+    from test_oracle_golden import G, c32_of
+    g = G["reciprocal_c32"]
+    zs = np.array([c32_of(e["z"]) for e in g["exact"]], np.complex64)
+    got = gpu_rcp_c32(ctx, zs).view(np.uint32).reshape(-1, 2)
+    want = np.array([[int(e["w"][0], 16), int(e["w"][1], 16)] for e in g["exact"]], np.uint32)
+    assert (got == want).all(), np.argwhere(got != want)[:5]
+    nz = np.array([c32_of(p) for p in g["nan_inputs"]], np.complex64)
+    assert (gpu_rcp_c32(ctx, nz).view(np.uint32) == 0x7FC00000).all()
+
+
+@pytest.mark.parametrize("seed,lo,hi,spread", [(10, 87, 167, 80), (11, 87, 167, 2), (12, -22, 254, 276),
+                                               (20, 245, 254, 9), (30, -22, 3, 25), (31, -22, 60, 82)])
+def test_complex_reciprocal_bit_exact_and_gate(ctx, seed, lo, hi, spread):
+    """300,000 inputs per family (moderate, comparable parts, full range, near overflow, near
+    underflow): bit for bit the oracle's split-float Smith algorithm, and within the reference's
+    accuracy gate against the f64 value."""
+    from test_oracle_golden import complex_inputs, assert_complex_gate
+    z = complex_inputs(seed + 100, 300_000, lo, hi, spread)
+    got = gpu_rcp_c32(ctx, z)
+    want = O.reciprocal_c32(z)
+    assert (got.view(np.uint32) == want.view(np.uint32)).all()
+    assert_complex_gate(z, got)
+
+
+def test_complex_reciprocal_specials_and_real_axis(ctx):
+    """Zero, infinite and NaN parts in every sign combination, and 1/(x + 0i) on the real axis
+    equal to the real reciprocal with imaginary part -0 (tests/reciprocal_test.rs:745-760)."""
+    specials = SPECIALS.view(np.float32)
+    re, im = np.meshgrid(specials, specials)
+    z = np.empty(re.size, np.complex64)
+    z.real, z.imag = re.ravel(), im.ravel()
+    got = gpu_rcp_c32(ctx, z)
+    assert (got.view(np.uint32) == O.reciprocal_c32(z).view(np.uint32)).all()
+    from test_oracle_golden import fields_to_f32
+    x = fields_to_f32(np.random.default_rng(40), np.random.default_rng(41).integers(-22, 255, 100_000))
+    w = gpu_rcp_c32(ctx, x.astype(np.complex64))
+    assert (w.real.view(np.uint32) == O.reciprocal(x).view(np.uint32)).all()
+    assert (w.imag.view(np.uint32) == 0x80000000).all()
+
+
+def test_complex_reciprocal_layouts(ctx):
+    """Strided (every other element), a misaligned start and an odd count (no 16-byte vectors),
+    in place, and a batched diagonal view: each element gets its own reciprocal."""
+    from test_oracle_golden import complex_inputs
+    z = complex_inputs(50, 4001, 100, 150, 10)
+    base = dev(z)
+    want = O.reciprocal_c32(z)
+    # every other element into a dense buffer
+    sv = lb.View.raw(base, 0, [2001], [2])
+    out = torch.zeros(2001, dtype=torch.complex64, device="cuda")
+    lb.reciprocal(ctx, sv, out)
+    assert (out.cpu().numpy().view(np.uint32) == np.ascontiguousarray(want[::2]).view(np.uint32)).all()
+    # misaligned start (offset 1: 8-byte aligned only), odd count, out of place
+    mv = lb.View.raw(base, 1, [3999], [1])
+    out2 = torch.zeros(3999, dtype=torch.complex64, device="cuda")
+    lb.reciprocal(ctx, mv, out2)
+    assert (out2.cpu().numpy().view(np.uint32) == want[1:4000].view(np.uint32)).all()
+    # the diagonals of a batch of 7 x 7 matrices, in place
+    m = complex_inputs(51, 5 * 49, 100, 150, 10)
+    mt = dev(m)
+    diag = lb.View.raw(mt, 0, [5, 7], [49, 8])
+    lb.reciprocal(ctx, diag, diag)
+    got = mt.cpu().numpy().reshape(5, 7, 7)
+    ref = m.reshape(5, 7, 7).copy()
+    idx = np.arange(7)
+    ref[:, idx, idx] = O.reciprocal_c32(ref[:, idx, idx].ravel()).reshape(5, 7)
+    assert (got.view(np.uint32) == ref.view(np.uint32)).all()
+
+
+# ------------------------------------------------------------------------------------------------
 # permutation
 # ------------------------------------------------------------------------------------------------
 

@@ -201,6 +201,81 @@ def test_sqrt_and_reciprocal_goldens():
     assert [bits_of(v) for v in O.reciprocal(xs)] == [int(b, 16) for _, b in G["reciprocal"]["cases"]]
 
 
+def c32_of(pair) -> np.complex64:
+    return np.array([int(pair[0], 16), int(pair[1], 16)], np.uint32).view(np.complex64)[0]
+
+
+def test_complex_reciprocal_goldens():
+    """Every exact complex result the reference's reciprocal tests assert, and the NaN rule."""
+    g = G["reciprocal_c32"]
+    zs = np.array([c32_of(e["z"]) for e in g["exact"]], np.complex64)
+    ws = O.reciprocal_c32(zs).view(np.uint32).reshape(-1, 2)
+    for e, w in zip(g["exact"], ws):
+        assert [int(w[0]), int(w[1])] == [int(e["w"][0], 16), int(e["w"][1], 16)], e
+    nz = np.array([c32_of(p) for p in g["nan_inputs"]], np.complex64)
+    assert (O.reciprocal_c32(nz).view(np.uint32) == 0x7FC00000).all()
+
+
+def fields_to_f32(rng, fields):
+    """Random-signed floats whose magnitudes lie in [2^(f-127), 2^(f-126)) for biased exponent
+    field f, extended below 1 to subnormals (tests/reciprocal_test.rs:264-278, own generator)."""
+    fields = np.asarray(fields, np.int64)
+    frac = rng.integers(0, 1 << 23, size=fields.shape, dtype=np.int64)
+    top = np.left_shift(1, np.clip(22 + fields, 0, 22))
+    mag = np.where(fields >= 1, (np.clip(fields, 1, 254) << 23) | frac, top | (frac & (top - 1)))
+    sign = rng.integers(0, 2, size=fields.shape, dtype=np.int64) << 31
+    return (mag | sign).astype(np.uint32).view(np.float32)
+
+
+def complex_inputs(seed, count, lo, hi, spread):
+    rng = np.random.default_rng(seed)
+    re = rng.integers(lo, hi + 1, size=count)
+    im = rng.integers(np.maximum(lo, re - spread), np.minimum(hi, re + spread) + 1)
+    z = np.empty(count, np.complex64)
+    z.real, z.imag = fields_to_f32(rng, re), fields_to_f32(rng, im)
+    return z
+
+
+def ulp_distance(got: np.ndarray, want: np.ndarray) -> np.ndarray:
+    """f32 distance with infinity next to the largest finite value; NaN matches only NaN and
+    the signs (zero's too) must agree, else a huge distance (tests/reciprocal_test.rs:148-158)."""
+    gb, wb = got.view(np.uint32).astype(np.int64), want.view(np.uint32).astype(np.int64)
+    d = np.abs((gb & 0x7FFFFFFF) - (wb & 0x7FFFFFFF))
+    both_nan = np.isnan(got) & np.isnan(want)
+    bad = (np.isnan(got) != np.isnan(want)) | ((gb >> 31) != (wb >> 31))
+    return np.where((gb == wb) | both_nan, 0, np.where(bad, 1 << 40, d))
+
+
+def assert_complex_gate(z: np.ndarray, w: np.ndarray):
+    """The reference's accuracy gate for finite nonzero z (tests/reciprocal_test.rs:187-229):
+    normwise error <= 4u |1/z| + 2^-149 against the f64 value, each part within 4 ulps of it."""
+    a, b = z.real.astype(np.float64), z.imag.astype(np.float64)
+    n2 = a * a + b * b
+    want = [a / n2, -b / n2]
+    got = [w.real, w.imag]
+    delta, ulps = [], np.zeros(len(z), np.int64)
+    for c in range(2):
+        with np.errstate(over="ignore"):  # results past the f32 range round to infinity
+            rounded = want[c].astype(np.float32)
+        ulps = np.maximum(ulps, ulp_distance(got[c], rounded))
+        g = got[c].astype(np.float64)
+        delta.append(np.where(~np.isinf(g), g - want[c],
+                              np.where(np.isinf(rounded), 0.0, np.copysign(2.0 ** 128, g) - want[c])))
+    absolute = np.hypot(delta[0], delta[1])
+    modulus = np.hypot(want[0], want[1])
+    ok = (ulps <= 4) & (absolute <= 4.0 * 2.0 ** -24 * modulus + 2.0 ** -149)
+    assert ok.all(), (z[~ok][:4], w[~ok][:4])
+
+
+@pytest.mark.parametrize("seed,lo,hi,spread", [(10, 87, 167, 80), (11, 87, 167, 2), (12, -22, 254, 276),
+                                               (20, 245, 254, 9), (30, -22, 3, 25), (31, -22, 60, 82)])
+def test_complex_reciprocal_oracle_meets_gate(seed, lo, hi, spread):
+    """The restatement meets the reference's accuracy gate on the input families of its tests
+    (moderate, comparable parts, full range, near overflow, near underflow)."""
+    z = complex_inputs(seed, 20_000, lo, hi, spread)
+    assert_complex_gate(z, O.reciprocal_c32(z))
+
+
 def test_wire_goldens():
     w = G["wire"]
     for c in w["roundtrip"]:
