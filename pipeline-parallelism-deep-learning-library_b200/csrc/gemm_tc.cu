@@ -485,6 +485,54 @@ __device__ __forceinline__ void store_tile32(const KParams& p, const float (&v)[
   }
 }
 
+// Fused-SGD epilogue, software-pipelined over the 32-column groups of a row block: the master
+// weights of group g + 1 are loaded (into `next`) before group g is computed, so their load
+// latency overlaps a whole group's TMEM read, transpose and stores instead of stalling every
+// group (measured: 2.3 us per group with the loads issued in-line).  Lane layout as in
+// store_tile32: lane = 8 * (row % 4) + column quad, rows 4 i + lane / 8.
+__device__ __forceinline__ void load_master_block(const KParams& p, int64_t base, int32_t rows, float (&o)[8][4]) {
+  const int lane = threadIdx.x & 31;
+  const int rr = lane >> 3, cc = (lane & 7) * 4;
+#pragma unroll
+  for (int i = 0; i < 8; i++) {
+    float4 t = make_float4(0.f, 0.f, 0.f, 0.f);
+    if (4 * i + rr < rows)
+      t = __ldcs(reinterpret_cast<const float4*>(static_cast<const float*>(p.aux) + base + (int64_t)(4 * i + rr) * p.c_ms + cc));
+    o[i][0] = t.x;
+    o[i][1] = t.y;
+    o[i][2] = t.z;
+    o[i][3] = t.w;
+  }
+}
+
+__device__ __forceinline__ void sgd_block32(const KParams& p, const uint32_t (&r)[32], float* stage, int64_t base,
+                                            int32_t rows, const float (&o)[8][4]) {
+  const int lane = threadIdx.x & 31;
+  __syncwarp();  // the previous block has been read out of the tile
+  float4* mine = reinterpret_cast<float4*>(stage + lane * 36);
+#pragma unroll
+  for (int k = 0; k < 8; k++)
+    mine[k] = make_float4(__uint_as_float(r[4 * k]), __uint_as_float(r[4 * k + 1]), __uint_as_float(r[4 * k + 2]),
+                          __uint_as_float(r[4 * k + 3]));
+  __syncwarp();
+  const int rr = lane >> 3, cc = (lane & 7) * 4;
+#pragma unroll
+  for (int i = 0; i < 8; i++) {
+    if (4 * i + rr >= rows) continue;
+    const float4 t = *reinterpret_cast<const float4*>(stage + (4 * i + rr) * 36 + cc);
+    const float x[4] = {t.x, t.y, t.z, t.w};
+    float out[4];
+#pragma unroll
+    for (int e = 0; e < 4; e++) out[e] = __fsub_rn(o[i][e], __fmul_rn(p.lr, __fmul_rn(p.alpha, x[e])));
+    const int64_t idx = base + (int64_t)(4 * i + rr) * p.c_ms + cc;
+    __stcs(reinterpret_cast<float4*>(static_cast<float*>(const_cast<void*>(p.aux)) + idx),
+           make_float4(out[0], out[1], out[2], out[3]));
+    __stcs(reinterpret_cast<uint2*>(static_cast<uint16_t*>(p.aux2) + idx),
+           make_uint2(f32_to_bf16_rne(out[0]) | ((uint32_t)f32_to_bf16_rne(out[1]) << 16),
+                      f32_to_bf16_rne(out[2]) | ((uint32_t)f32_to_bf16_rne(out[3]) << 16)));
+  }
+}
+
 __device__ __forceinline__ float* partial_row(const KParams& p, int32_t split, int32_t b, int32_t m) {
   return p.partial + (((int64_t)split * p.batch + b) * p.M + m) * (int64_t)p.N;
 }
@@ -658,7 +706,8 @@ __device__ __forceinline__ void gemm_body(const Src& src) {
     }
     for (int a = 0; a < 2; a++) {
       lcd::mbar_init(&tfull[a], 1);
-      lcd::mbar_init(&tempty[a], TWO_SM ? 256 : 128);  // 2-SM: both CTAs' epilogue threads, on the leader
+      // one arrival per epilogue warp (2-SM: both CTAs' warps, on the leader)
+      lcd::mbar_init(&tempty[a], TWO_SM ? 8 : 4);
     }
     lcd::mbar_init(drain, 1);
     lcd::mbar_init(recv_full, 128);
@@ -975,7 +1024,8 @@ __device__ __forceinline__ void gemm_body(const Src& src) {
           }
           first = false;
           lcd::tc_fence_before();
-          lcd::mbar_arrive(&tempty[acc]);
+          __syncwarp();
+          if (lane == 0) lcd::mbar_arrive(&tempty[acc]);
         }
         if (!ok) break;
         // every conversion of this unit preceded its last hand-off, so its stamp is in place
@@ -1083,10 +1133,19 @@ __device__ __forceinline__ void gemm_body(const Src& src) {
         }
         lcd::mbar_arrive_remote(lcd::mapa_shared(lcd::smem_u32(recv_free), peer));
         lcd::tc_fence_before();
-        lcd::mbar_arrive(&tempty[acc]);
+        __syncwarp();
+        if (lane == 0) lcd::mbar_arrive(&tempty[acc]);
         h++;
       } else {
         const int acc = h & 1;
+        // fused SGD over whole 32-column groups: the first group's master weights do not depend
+        // on the accumulator, so they are loaded while the MMAs finish
+        const int32_t m0w = tile_row0(tm) + q * 32;
+        const int32_t rows = min(32, p.M - m0w);
+        const bool sgd_pipe = EPI == 2 && !split_mode && p.vec && tn * BN + BN <= p.N && rows > 0;
+        const int64_t base0 = p.c_off + (int64_t)b * p.c_bs + (int64_t)m0w * p.c_ms + tn * BN;
+        float next[8][4];
+        if (sgd_pipe) load_master_block(p, base0, rows, next);
         if (!lcd::mbar_wait(&tfull[acc], (h >> 1) & 1, p.err)) {
           ok = false;
           break;
@@ -1107,17 +1166,39 @@ __device__ __forceinline__ void gemm_body(const Src& src) {
             for (int32_t off = 0; off < bytes; off += 128) asm volatile("prefetch.global.L2 [%0];" ::"l"(src + off));
           }
         }
+        if (sgd_pipe) {
+          float* stage = epi_stage + (warp - 2) * (32 * 36);
+          float o[8][4];
 #pragma unroll 1
-        for (int g = 0; g < BN / 32; g++) {
-          uint32_t r[32];
-          lcd::tmem_ld_32x32b_x32(lane_base + acc * BN + g * 32, r);
-          lcd::tmem_ld_wait();
-          emit(r, tn * BN + g * 32);
+          for (int g = 0; g < BN / 32; g++) {
+#pragma unroll
+            for (int i = 0; i < 8; i++)
+#pragma unroll
+              for (int e = 0; e < 4; e++) o[i][e] = next[i][e];
+            if (g + 1 < BN / 32) load_master_block(p, base0 + (g + 1) * 32, rows, next);
+            uint32_t r[32];
+            lcd::tmem_ld_32x32b_x32(lane_base + acc * BN + g * 32, r);
+            lcd::tmem_ld_wait();
+            sgd_block32(p, r, stage, base0 + g * 32, rows, o);
+          }
+        } else {
+#pragma unroll 1
+          for (int g = 0; g < BN / 32; g++) {
+            uint32_t r[32];
+            lcd::tmem_ld_32x32b_x32(lane_base + acc * BN + g * 32, r);
+            lcd::tmem_ld_wait();
+            emit(r, tn * BN + g * 32);
+          }
         }
         lcd::tc_fence_before();
-        // TWO_SM: the leader's MMAs refill both CTAs' accumulators, so both release on its barrier
-        if (TWO_SM && rank == 1) lcd::mbar_arrive_remote(lcd::leader_addr(lcd::smem_u32(&tempty[acc])));
-        else lcd::mbar_arrive(&tempty[acc]);
+        // TWO_SM: the leader's MMAs refill both CTAs' accumulators, so both release on its
+        // barrier.  One arrival per warp once every lane's TMEM reads are done (128 remote
+        // arrivals per unit from the peer held the leader's next MMAs back by 2-4 us)
+        __syncwarp();
+        if (lane == 0) {
+          if (TWO_SM && rank == 1) lcd::mbar_arrive_remote(lcd::leader_addr(lcd::smem_u32(&tempty[acc])));
+          else lcd::mbar_arrive(&tempty[acc]);
+        }
         h++;
       }
       if (split_mode && p.fixup) {
