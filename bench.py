@@ -299,6 +299,18 @@ def run_profile(args):
         ctx.sync()
         print(json.dumps({"profile": "gemm", "launches": ctx.debug_launches()[-8:]}))
         return 0
+    if args.profile == "square":
+        # --warmup + --steps back-to-back 8192^3 bf16 products (the gemm_bf16_8192 figure)
+        ctx = lb.Context(0)
+        n = 8192
+        a = torch.randn(n, n, device="cuda").bfloat16()
+        b = torch.randn(n, n, device="cuda").bfloat16()
+        c = torch.empty(n, n, device="cuda", dtype=torch.bfloat16)
+        for _ in range(args.warmup + args.steps):
+            lb.encode_gemm(ctx, ctx.stream, 1.0, a, b, 0.0, c)
+        ctx.sync()
+        print(json.dumps({"profile": "square", "launches": ctx.debug_launches()[-1:]}))
+        return 0
     if args.profile == "ops":
         # one round = slice+pack, bf16 split-K, f32 split-K (3xTF32), argmax over the last axis,
         # permute (0,3,1,2), sqrt: the configs of the op figures, in that launch order
@@ -349,11 +361,12 @@ def main():
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--no-extras", action="store_true", help="skip the N=1 contraction/op figures")
     ap.add_argument("--layers", type=int, default=LAYERS, help="profiling driver only: pipeline depth")
-    ap.add_argument("--profile", choices=["step", "gemm", "ops"], default=None,
+    ap.add_argument("--profile", choices=["step", "gemm", "ops", "square"], default=None,
                     help="profiling driver: 'step' runs --warmup + --steps pipeline steps and nothing else; "
                          "'gemm' runs --steps forward-shaped GEMMs ([64,8192] x [8192,8192] bf16); "
                          "'ops' runs --warmup + --steps rounds of the op-figure configs (pack, bf16 and "
-                         "f32 split-K, argmax rows, permute, sqrt)")
+                         "f32 split-K, argmax rows, permute, sqrt); 'square' runs --warmup + --steps "
+                         "8192^3 bf16 products")
     args = ap.parse_args()
     if args.impl == "reference":
         return run_reference(args)
