@@ -100,6 +100,11 @@ const char* lc_last_error(void);
 uint64_t lc_debug_launches(lc_context* ctx);
 /* Kernel name of launch `index` (0-based) for the most recent 4096 launches, or NULL. */
 const char* lc_debug_launch_name(lc_context* ctx, uint64_t index);
+/* Failure-detection probe (no reference counterpart): enqueues a one-warp kernel that waits,
+ * through the bounded wait every library kernel uses, on a barrier nothing arrives on; after
+ * `limit_us` (1 us .. 4 s) it gives up and raises the device error word, so the next lc_sync
+ * returns LC_ERR_DEVICE_TIMEOUT and clears it.  No GPU fault, trap or hang is involved. */
+lc_status lc_debug_wait_probe(lc_context* ctx, void* stream, uint32_t limit_us);
 
 /* ---- views (host-only metadata; src/abi.rs:102-211, src/ops/permutation.rs:295-320,
  *      src/ops/slicing.rs:471-514) ------------------------------------------------------- */

@@ -2146,3 +2146,37 @@ lc_status gemm_fill(lc_context* ctx, cudaStream_t s, const GemmProblem& pr) {
 }
 
 }  // namespace lc
+
+// ---- failure detection: a bounded wait that can only run out ------------------------------------
+namespace {
+
+// One warp waits on an mbarrier that nothing ever arrives on, through the same bounded wait the
+// GEMM kernels use (here with a short limit): it gives up, raises the device error word and
+// returns, so the host sees LC_ERR_DEVICE_TIMEOUT at its next lc_sync and the context stays
+// usable.
+__global__ void __launch_bounds__(32) wait_probe_kernel(int* err, uint64_t limit_ns) {
+  __shared__ __align__(8) uint64_t bar;
+  if (threadIdx.x == 0) {
+    lcd::mbar_init(&bar, 1);
+    lcd::fence_mbar_init();
+  }
+  __syncwarp();
+  lcd::mbar_wait(&bar, 0, err, limit_ns);
+}
+
+}  // namespace
+
+extern "C" {
+
+lc_status lc_debug_wait_probe(lc_context* ctx, void* stream, uint32_t limit_us) {
+  using namespace lc;
+  if (ctx == nullptr) return fail(LC_ERR_INVALID_ARGUMENT, "null context");
+  if (limit_us == 0 || limit_us > 4000000u) return fail(LC_ERR_INVALID_ARGUMENT, "wait probe limit must be 1 us .. 4 s");
+  wait_probe_kernel<<<1, 32, 0, stream_of(ctx, stream)>>>(ctx->d_error, (uint64_t)limit_us * 1000ull);
+  record_launch(ctx, "debug_wait_probe");
+  cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess) return cuda_fail(e, "wait probe launch");
+  return LC_OK;
+}
+
+}  // extern "C"

@@ -70,7 +70,8 @@ __device__ __forceinline__ bool mbar_try_wait(uint32_t bar_addr, uint32_t parity
 
 // Bounded wait for the phase of parity `parity` to complete.  Returns false (and raises the
 // device error word) when the limit passes first.
-__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, int* err) {
+__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, int* err,
+                                          uint64_t limit_ns = kWaitLimitNs) {
   const uint32_t a = smem_u32(bar);
   if (mbar_try_wait(a, parity)) return true;
   const uint64_t t0 = global_ns();
@@ -78,7 +79,7 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, int* e
     if (mbar_try_wait(a, parity)) return true;
     if ((i & 255u) == 0) {
       if (err != nullptr && *(volatile int*)err != 0) return false;  // another CTA gave up
-      if (global_ns() - t0 > kWaitLimitNs) {
+      if (global_ns() - t0 > limit_ns) {
         if (err != nullptr) atomicOr(err, 1);
         return false;
       }

@@ -94,6 +94,7 @@ def _sig(L):
         "lc_last_error": (C.c_char_p, []),
         "lc_debug_launches": (C.c_uint64, [_vp]),
         "lc_debug_launch_name": (C.c_char_p, [_vp, C.c_uint64]),
+        "lc_debug_wait_probe": (C.c_int, [_vp, _vp, C.c_uint32]),
         "lc_view_validate": (s, [_V]),
         "lc_permute_view": (s, [_V, C.POINTER(C.c_int32), C.c_int32, _V]),
         "lc_slice": (s, [_V, C.POINTER(C.c_uint64), C.POINTER(C.c_uint64), C.c_int32, _V]),
@@ -283,6 +284,10 @@ class Context:
 
     def sync(self, stream=None):
         check(load().lc_sync(self.h, stream))
+
+    def debug_wait_probe(self, limit_us: int, stream=None):
+        """Enqueue a kernel whose bounded wait can only run out (failure-detection test)."""
+        check(load().lc_debug_wait_probe(self.h, stream, limit_us))
 
     def debug_launches(self) -> list[str]:
         L = load()

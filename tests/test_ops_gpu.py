@@ -601,6 +601,25 @@ def test_contract_determinism(ctx):
 # Backend training ops
 # ------------------------------------------------------------------------------------------------
 
+def test_bounded_wait_runs_out_and_context_recovers(gpu):
+    """Failure detection without a GPU fault: a kernel waits, through the library's bounded wait,
+    on a barrier nothing arrives on; after 50 ms it gives up and raises the device error word,
+    lc_sync reports LC_ERR_DEVICE_TIMEOUT, and the same context then runs a product correctly."""
+    c = lb.Context(0)
+    c.debug_wait_probe(50_000)
+    with pytest.raises(lb.DeviceTimeout):
+        c.sync()
+    c.sync()  # the error word was cleared
+    a = torch.randn(256, 512, device="cuda")
+    b = torch.randn(512, 128, device="cuda")
+    out = torch.empty(256, 128, device="cuda")
+    lb.contract(c, 1.0, (a, "ik"), (b, "kj"), 0.0, (out, "ij"))
+    ref = a.double() @ b.double()
+    assert ((out.double() - ref).abs().max() / ref.abs().max()).item() <= F32_TOL
+    with pytest.raises(lb.InvalidArgument):
+        c.debug_wait_probe(0)
+
+
 def test_training_ops_match_oracle(ctx):
     x = data.normal(1, (37, 91))
     bvec = data.normal(2, (91,))
