@@ -1728,39 +1728,59 @@ lc_status plan_gemm(lc_context* ctx, const lc::GemmProblem& pr, lc_contract_plan
   const int epr = tf32x3 ? 32 : 64;
   const size_t es = dtype_size(pr.in_dtype);
   int bn = N <= 64 ? 64 : (N <= 128 || tf32x3) ? 128 : 256;
-  const int64_t tiles_m = ceil_div(M, 128), tiles_n = ceil_div(N, bn);
+  const int64_t tiles_m = ceil_div(M, 128);
   const int64_t k_tiles = ceil_div(pr.k, epr);
-  const int64_t tiles = tiles_m * tiles_n * pr.batch;
   // Split-K choice: the CTAs are persistent, one per SM, so a unit count just above a multiple
   // of the SM count costs a whole extra wave.  Cost of s splits, in k-tile times along the
   // critical path: waves(s) * (k-tiles per unit + the unit's partial write and reduce read,
   // expressed in k-tile loads).  The cheapest s wins; ties go to fewer splits.
   const int64_t sms = std::max<int64_t>(1, ctx->sm_count - pr.reserve_sms);
-  const double tile_load = (double)(128 + bn) * 128.0;
-  const double partial_cost = (128.0 * bn * 4.0 * 2.0) / tile_load;
-  auto split_cost = [&](int64_t s) {
-    const int64_t per = ceil_div(k_tiles, s);
-    const int64_t real = ceil_div(k_tiles, per);
-    const int64_t waves = ceil_div(tiles * real, sms);
-    return (double)waves * ((double)per + (real > 1 ? partial_cost : 0.0));
-  };
-  int64_t splits = 1, kps = k_tiles;
   static const int64_t env_splits = [] {
     const char* e = getenv("LC_SPLITK");  // tuning override for sweeps; unset in normal use
     return e ? atoll(e) : 0ll;
   }();
-  if (pr.splits_hint > 0 || env_splits > 0) {
-    splits = std::min<int64_t>(pr.splits_hint > 0 ? pr.splits_hint : env_splits, k_tiles);
-  } else {
+  auto best_split = [&](int bn_try, int64_t* s_out) -> double {
+    const int64_t t = tiles_m * ceil_div(N, bn_try) * pr.batch;
+    const double partial_cost = (128.0 * bn_try * 4.0 * 2.0) / ((double)(128 + bn_try) * 128.0);
+    auto split_cost = [&](int64_t sp) {
+      const int64_t per = ceil_div(k_tiles, sp);
+      const int64_t real = ceil_div(k_tiles, per);
+      const int64_t waves = ceil_div(t * real, sms);
+      return (double)waves * ((double)per + (real > 1 ? partial_cost : 0.0));
+    };
+    int64_t sp = 1;
     double best = split_cost(1);
-    for (int64_t s = 2; s <= std::min<int64_t>(k_tiles, 512); s++) {
-      const double c = split_cost(s);
-      if (c < best * 0.999) {
-        best = c;
-        splits = s;
+    if (pr.splits_hint > 0 || env_splits > 0) {
+      sp = std::max<int64_t>(1, std::min<int64_t>(pr.splits_hint > 0 ? pr.splits_hint : env_splits, k_tiles));
+      best = split_cost(sp);
+    } else {
+      for (int64_t c = 2; c <= std::min<int64_t>(k_tiles, 512); c++) {
+        const double v = split_cost(c);
+        if (v < best * 0.999) {
+          best = v;
+          sp = c;
+        }
       }
     }
+    *s_out = sp;
+    return best;
+  };
+  int64_t splits = 1, kps = k_tiles;
+  const double cost = best_split(bn, &splits);
+  // 3xTF32: a 128 x 64 tile's k-tile takes about 0.6 of a 128 x 128 one (the converters' and the
+  // MMAs' work on B halves, on A it does not), so the narrower tile wins when it spares a split
+  // or a wave: the 1024^3 product runs unsplit on 128 x 64 tiles in 31.8 us, against 36.1 us
+  // with two splits on 128 x 128 (same-box timings)
+  if (tf32x3 && bn == 128) {
+    int64_t s64 = 1;
+    const double c64 = 0.6 * best_split(64, &s64);
+    if (c64 < cost * 0.999) {
+      bn = 64;
+      splits = s64;
+    }
   }
+  const int64_t tiles_n = ceil_div(N, bn);
+  const int64_t tiles = tiles_m * tiles_n * pr.batch;
   splits = std::max<int64_t>(splits, 1);
   kps = ceil_div(k_tiles, splits);
   splits = ceil_div(k_tiles, kps);

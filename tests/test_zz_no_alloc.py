@@ -37,7 +37,7 @@ def _operands(m, n, k, dtype, seed):
 # product that does not split.
 CASES = [
     (64, 8192, 8192, torch.bfloat16, 1.0, 0.0, ("Split", 2)),
-    (1024, 1024, 1024, torch.float32, 0.5, 0.25, ("Split", 2)),
+    (1024, 1024, 2048, torch.float32, 0.5, 0.25, ("Split", 2)),
     (256, 256, 65536, torch.float32, 1.0, -1.5, ("Split", 37)),
     (2048, 2048, 256, torch.bfloat16, 1.0, 1.0, ("Tiled", 1)),
 ]
