@@ -190,8 +190,24 @@ __global__ void __launch_bounds__(256) transpose_kernel(const E* __restrict__ sr
     E* d = dst + g.dst_off + dof;
     const bool full_a = a0 + T <= g.ext_a, full_b = b0 + T <= g.ext_b;
     const int tx = threadIdx.x % VPR, ty = threadIdx.x / VPR;
-    // load: tile[bb][aa] = src[(a0+aa) + (b0+bb)*stride_b]
-    for (int bb = ty; bb < T; bb += RPP) {
+    // load: tile[bb][aa] = src[(a0+aa) + (b0+bb)*stride_b].  A whole, 16-byte aligned tile
+    // issues all of a thread's T / RPP vector loads before its first shared-memory store.
+    const bool whole = full_a && b0 + T <= g.ext_b &&
+                       reinterpret_cast<uintptr_t>(s + b0 * g.src_stride_b + a0) % 16 == 0 &&
+                       (g.src_stride_b * sizeof(E)) % 16 == 0;
+    if (whole) {
+      uint4 v[T / RPP];
+#pragma unroll
+      for (int k = 0; k < T / RPP; k++)
+        v[k] = __ldcs(reinterpret_cast<const uint4*>(s + (b0 + ty + k * RPP) * g.src_stride_b + a0) + tx);
+#pragma unroll
+      for (int k = 0; k < T / RPP; k++) {
+        const E* e = reinterpret_cast<const E*>(&v[k]);
+#pragma unroll
+        for (int u = 0; u < V; u++) tile[ty + k * RPP][tx * V + u] = e[u];
+      }
+    }
+    for (int bb = ty; bb < T && !whole; bb += RPP) {
       const uint64_t b = b0 + bb;
       const E* row = s + b * g.src_stride_b + a0;
       if (full_a && b < g.ext_b && (reinterpret_cast<uintptr_t>(row) % 16 == 0)) {
