@@ -43,7 +43,7 @@ using namespace lc;
 // same soname in one process would otherwise race for the symbols at load time.
 struct NcclApi {
   ncclResult_t (*GetUniqueId)(ncclUniqueId*) = nullptr;
-  ncclResult_t (*CommInitRank)(ncclComm_t*, int, ncclUniqueId, int) = nullptr;
+  ncclResult_t (*CommInitRankConfig)(ncclComm_t*, int, ncclUniqueId, int, ncclConfig_t*) = nullptr;
   ncclResult_t (*CommSplit)(ncclComm_t, int, int, ncclComm_t*, ncclConfig_t*) = nullptr;
   ncclResult_t (*CommDestroy)(ncclComm_t) = nullptr;
   ncclResult_t (*CommAbort)(ncclComm_t) = nullptr;
@@ -65,7 +65,7 @@ const NcclApi& nccl() {
       fn = reinterpret_cast<std::remove_reference_t<decltype(fn)>>(dlsym(h, name));
       return fn != nullptr;
     };
-    api.ok = sym(api.GetUniqueId, "ncclGetUniqueId") && sym(api.CommInitRank, "ncclCommInitRank") &&
+    api.ok = sym(api.GetUniqueId, "ncclGetUniqueId") && sym(api.CommInitRankConfig, "ncclCommInitRankConfig") &&
              sym(api.CommSplit, "ncclCommSplit") && sym(api.CommDestroy, "ncclCommDestroy") &&
              sym(api.CommAbort, "ncclCommAbort") && sym(api.CommGetAsyncError, "ncclCommGetAsyncError") &&
              sym(api.Send, "ncclSend") && sym(api.Recv, "ncclRecv") && sym(api.GetErrorString, "ncclGetErrorString");
@@ -93,6 +93,7 @@ __global__ void to_bf16_kernel(const float* __restrict__ x, uint16_t* __restrict
 //   d = f32(y) - t;  part += d*d;  g = (y > 0) ? bf16((2*d)/N) : 0
 constexpr int kMseThreads = 256;
 constexpr int kMseBlocks = 296;  // 2 per SM: the loss gradient of one microbatch in one wave
+constexpr int kNcclCtas = 2;     // CTAs per NCCL transfer kernel (communicator maxCTAs)
 // dy = relu'(y) * (2 * (y - t)) / n and per-block partial sums of (y - t)^2, 8 elements at a time
 // (16-byte loads of y and g, two of t); the partials are summed in a fixed order by
 // loss_reduce_kernel, so the loss is deterministic.
@@ -619,8 +620,23 @@ lc_status lc_pipeline_create(const lc_pipeline_config* cfg, const uint8_t id[LC_
       lc_pipeline_destroy(p);
       return fail(LC_ERR_TRANSPORT, "libnccl.so.2 could not be loaded");
     }
-    ncclResult_t r = nccl().CommInitRank(&p->comm_fwd, world, u, rank);
-    if (r == ncclSuccess) r = nccl().CommSplit(p->comm_fwd, 0, rank, &p->comm_bwd, nullptr);
+    // NCCL's transfer kernels share the GPU with the layer chains, which are cooperative launches
+    // sized to leave 4 SMs free.  A receive is posted before its data exists and spins until the
+    // peer sends; if its CTAs sit on SMs a chain needs, that chain cannot start until the
+    // transfer ends, and the stall passes from stage to stage.  At most two NCCL kernels run at
+    // once (one per communicator: forward and backward), so two CTAs each fit the free SMs.
+    static const int env_ctas = [] {
+      const char* e = getenv("LC_PIPE_NCCL_CTAS");  // tuning override: CTAs per NCCL kernel, 0 = NCCL's choice
+      return e ? atoi(e) : -1;
+    }();
+    const int ctas = env_ctas >= 0 ? env_ctas : kNcclCtas;
+    ncclConfig_t cfg = NCCL_CONFIG_INITIALIZER;
+    if (ctas > 0) {
+      cfg.minCTAs = 1;
+      cfg.maxCTAs = ctas;
+    }
+    ncclResult_t r = nccl().CommInitRankConfig(&p->comm_fwd, world, u, rank, &cfg);
+    if (r == ncclSuccess) r = nccl().CommSplit(p->comm_fwd, 0, rank, &p->comm_bwd, &cfg);
     if (r != ncclSuccess) {
       lc_pipeline_destroy(p);
       return nccl_fail(r, "communicator setup");
