@@ -93,7 +93,7 @@ __global__ void to_bf16_kernel(const float* __restrict__ x, uint16_t* __restrict
 //   d = f32(y) - t;  part += d*d;  g = (y > 0) ? bf16((2*d)/N) : 0
 constexpr int kMseThreads = 256;
 constexpr int kMseBlocks = 296;  // 2 per SM: the loss gradient of one microbatch in one wave
-constexpr int kNcclCtas = 2;     // CTAs per NCCL transfer kernel (communicator maxCTAs)
+constexpr int kNcclCtas = 0;     // CTAs per NCCL transfer kernel (communicator maxCTAs); 0 = NCCL's choice
 // dy = relu'(y) * (2 * (y - t)) / n and per-block partial sums of (y - t)^2, 8 elements at a time
 // (16-byte loads of y and g, two of t); the partials are summed in a fixed order by
 // loss_reduce_kernel, so the loss is deterministic.
@@ -620,11 +620,10 @@ lc_status lc_pipeline_create(const lc_pipeline_config* cfg, const uint8_t id[LC_
       lc_pipeline_destroy(p);
       return fail(LC_ERR_TRANSPORT, "libnccl.so.2 could not be loaded");
     }
-    // NCCL's transfer kernels share the GPU with the layer chains, which are cooperative launches
-    // sized to leave 4 SMs free.  A receive is posted before its data exists and spins until the
-    // peer sends; if its CTAs sit on SMs a chain needs, that chain cannot start until the
-    // transfer ends, and the stall passes from stage to stage.  At most two NCCL kernels run at
-    // once (one per communicator: forward and backward), so two CTAs each fit the free SMs.
+    // NCCL's transfer kernels share the GPU with the layer chains (cooperative launches sized to
+    // leave 4 SMs free).  Capping them at two CTAs each, so that a spinning receive could never
+    // hold SMs a chain needs, measured no better on 2 B200s (59.6k samples/s either way) and
+    // slower on 4 (97.3k against 104.6k): NCCL keeps its own count unless LC_PIPE_NCCL_CTAS asks.
     static const int env_ctas = [] {
       const char* e = getenv("LC_PIPE_NCCL_CTAS");  // tuning override: CTAs per NCCL kernel, 0 = NCCL's choice
       return e ? atoi(e) : -1;
