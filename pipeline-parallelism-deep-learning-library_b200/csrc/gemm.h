@@ -28,6 +28,8 @@ struct GemmProblem {
   float alpha = 1.0f, beta = 0.0f;
   int32_t relu = 0;           // max(x, 0) after alpha/beta
   int32_t splits_hint = 0;    // 0 = choose
+  int32_t bn_hint = 0;        // 0 = choose; 64, 128 or 256 fixes the tile width (16-bit inputs only)
+  int32_t swap_hint = 0;      // 0 = choose; 1 = compute C^T = B^T A^T; -1 = never
   int32_t reserve_sms = 0;    // leave this many SMs free (for concurrent communication kernels)
   // Fused epilogues (the training step):
   //   epi 0  C = alpha*acc + beta*C (+ReLU)
@@ -72,6 +74,12 @@ lc_status gemm_run(lc_context* ctx, cudaStream_t s, const GemmProblem& p, lc_con
 // to launching the products one at a time with gemm_run.
 // `max_clusters` (> 0) caps the CTA pairs, leaving the rest of the SMs to work on another
 // stream (each pair then takes several tiles of a product).
+// The tile width, split count and orientation gemm_run would choose for `pr` (no launch, no
+// allocation), the orientation as 1 (C^T = B^T A^T) or -1.  Products over more rows that keep
+// the split count and orientation compute every output element with the same operations in the
+// same order (the tile width does not enter an element's arithmetic).
+lc_status gemm_plan_shape(lc_context* ctx, const GemmProblem& pr, int32_t* bn, int32_t* splits, int32_t* swap);
+
 lc_status gemm_chain_run(lc_context* ctx, cudaStream_t s, const GemmProblem* probs, int n, bool a_stable,
                          int max_clusters, bool* chained);
 

@@ -1709,6 +1709,7 @@ struct Planned {
   int bn = 64;
   bool tf32x3 = false, pair = false, two_sm = false;
   int64_t pair_clusters = 0, two_sm_clusters = 0, tiles = 0, units = 0, splits = 1, M = 0, N = 0;
+  bool swap = false;
 };
 
 lc_status plan_gemm(lc_context* ctx, const lc::GemmProblem& pr, lc_contract_plan* plan, bool dry_run, Planned* out) {
@@ -1718,7 +1719,7 @@ lc_status plan_gemm(lc_context* ctx, const lc::GemmProblem& pr, lc_contract_plan
   int64_t c_ms = pr.c_m_stride, c_ns = pr.c_n_stride;
   bool swap = false;
   // Skinny M: compute C^T = B^T A^T so the long side fills the 128-row MMA.
-  if (M < 128 && N > M) {
+  if (pr.swap_hint != 0 ? pr.swap_hint > 0 : (M < 128 && N > M)) {
     std::swap(A, B);
     std::swap(M, N);
     std::swap(c_ms, c_ns);
@@ -1728,6 +1729,7 @@ lc_status plan_gemm(lc_context* ctx, const lc::GemmProblem& pr, lc_contract_plan
   const int epr = tf32x3 ? 32 : 64;
   const size_t es = dtype_size(pr.in_dtype);
   int bn = N <= 64 ? 64 : (N <= 128 || tf32x3) ? 128 : 256;
+  if (!tf32x3 && (pr.bn_hint == 64 || pr.bn_hint == 128 || pr.bn_hint == 256)) bn = pr.bn_hint;
   const int64_t tiles_m = ceil_div(M, 128);
   const int64_t k_tiles = ceil_div(pr.k, epr);
   // Split-K choice: the CTAs are persistent, one per SM, so a unit count just above a multiple
@@ -1771,7 +1773,7 @@ lc_status plan_gemm(lc_context* ctx, const lc::GemmProblem& pr, lc_contract_plan
   // MMAs' work on B halves, on A it does not), so the narrower tile wins when it spares a split
   // or a wave: the 1024^3 product runs unsplit on 128 x 64 tiles in 31.8 us, against 36.1 us
   // with two splits on 128 x 128 (same-box timings)
-  if (tf32x3 && bn == 128) {
+  if (tf32x3 && bn == 128 && pr.bn_hint == 0) {
     int64_t s64 = 1;
     const double c64 = 0.6 * best_split(64, &s64);
     if (c64 < cost * 0.999) {
@@ -1928,6 +1930,7 @@ lc_status plan_gemm(lc_context* ctx, const lc::GemmProblem& pr, lc_contract_plan
   out->splits = splits;
   out->M = (int64_t)M;
   out->N = (int64_t)N;
+  out->swap = swap;
   return LC_OK;
 }
 
@@ -2061,6 +2064,16 @@ lc_status gemm_run(lc_context* ctx, cudaStream_t s, const GemmProblem& pr, lc_co
   return st;
 }
 
+lc_status gemm_plan_shape(lc_context* ctx, const GemmProblem& pr, int32_t* bn, int32_t* splits, int32_t* swap) {
+  Planned pl;
+  lc_status st = plan_gemm(ctx, pr, nullptr, false, &pl);
+  if (st) return st;
+  *bn = pl.bn;
+  *splits = (int32_t)pl.splits;
+  *swap = pl.swap ? 1 : -1;
+  return LC_OK;
+}
+
 lc_status gemm_chain_run(lc_context* ctx, cudaStream_t s, const GemmProblem* probs, int n, bool a_stable,
                          int max_clusters, bool* chained) {
   *chained = false;
@@ -2074,7 +2087,7 @@ lc_status gemm_chain_run(lc_context* ctx, cudaStream_t s, const GemmProblem* pro
   thread_local std::unique_ptr<ChainParams> cp_holder;
   if (!cp_holder) cp_holder.reset(new ChainParams());
   ChainParams& cp = *cp_holder;
-  int64_t clusters = 0;
+  int64_t clusters = 0, tiles = 0;
   for (int i = 0; i < n; i++) {
     if (probs[i].epi != epi) return LC_OK;
     Planned pl;
@@ -2085,11 +2098,14 @@ lc_status gemm_chain_run(lc_context* ctx, cudaStream_t s, const GemmProblem* pro
     cp.a[i] = pl.ta;
     cp.b[i] = pl.tb;
     clusters = std::max<int64_t>(clusters, pl.pair_clusters);
+    tiles = std::max<int64_t>(tiles, pl.tiles);
   }
   if (max_clusters > 0 && clusters > max_clusters) {
-    // as few waves as the cap allows, spread evenly over the pairs
-    const int64_t waves = ceil_div(clusters, max_clusters);
-    clusters = ceil_div(clusters, waves);
+    // as few waves as the cap allows, spread evenly over the pairs (counted in tiles, which can
+    // outnumber the pairs that fit at once)
+    const int64_t work = std::max<int64_t>(clusters, tiles);
+    const int64_t waves = ceil_div(work, max_clusters);
+    clusters = std::min<int64_t>(clusters, ceil_div(work, waves));
   }
   cp.n = n;
   cp.a_stable = a_stable ? 1 : 0;

@@ -93,6 +93,9 @@ __global__ void to_bf16_kernel(const float* __restrict__ x, uint16_t* __restrict
 //   d = f32(y) - t;  part += d*d;  g = (y > 0) ? bf16((2*d)/N) : 0
 constexpr int kMseThreads = 256;
 constexpr int kMseBlocks = 296;  // 2 per SM: the loss gradient of one microbatch in one wave
+// microbatches per product on a stage holding every layer: 32 x 8192 step on one B200, 55.4k
+// samples/s with 4 (256-row products), 48.2k with 2, 32.2k with 1
+constexpr uint64_t kFuseDefault = 4;
 constexpr int kNcclCtas = 0;     // CTAs per NCCL transfer kernel (communicator maxCTAs); 0 = NCCL's choice
 // dy = relu'(y) * (2 * (y - t)) / n and per-block partial sums of (y - t)^2, 8 elements at a time
 // (16-byte loads of y and g, two of t); the partials are summed in a fixed order by
@@ -245,6 +248,13 @@ struct lc_pipeline {
   std::vector<cudaEvent_t> ev_work_join;     // per extra compute stream: its last op of the step
   std::vector<cudaEvent_t> ev_fr, ev_fd, ev_br, ev_bd;
   std::vector<cudaEvent_t> ev_fdone;  // microbatch m's forward (and loss gradient) complete
+  // One stage holding every layer (training mode): consecutive microbatches run in groups of
+  // `fuse` as one product per layer, so one pass over a weight matrix serves the whole group.
+  struct Shape {
+    int32_t bn = 0, splits = 0, swap = 0;
+  };
+  uint64_t fuse = 0;  // 0 = not decided yet
+  std::vector<Shape> fwd_shape, dgrad_shape;
   float last_ms = 0.0f;
   bool aborted = false;
 
@@ -442,6 +452,59 @@ lc_status run_products(lc_pipeline* p, cudaStream_t s, const std::vector<GemmPro
   for (const GemmProblem& g : probs)
     if ((st = gemm_run(p->ctx, s, g, nullptr, false))) return st;
   return LC_OK;
+}
+
+// Microbatches per product.  Only a stage holding every layer in training mode groups them: its
+// 1F1B order is F(0) B(0) F(1) B(1) ..., the forwards only read weights nobody writes before the
+// step's weight updates, and B(m) needs nothing but F(m), so F(m) F(m+1) as one product followed
+// by B(m) B(m+1) as one product leaves every result unchanged (likewise for groups of four).
+// With several stages each microbatch crosses the link on its own and is computed alone.
+// LC_PIPE_FUSE=1 turns it off.
+lc_status decide_fuse(lc_pipeline* p) {
+  static const int env_fuse = [] {
+    const char* e = getenv("LC_PIPE_FUSE");  // microbatches per product on one stage (1, 2 or 4)
+    return e ? atoi(e) : 0;
+  }();
+  static const bool env_narrow = [] {
+    const char* e = getenv("LC_PIPE_GROUP_TILE");  // "0": keep the one-microbatch tile width
+    return e != nullptr && e[0] == '0';
+  }();
+  const uint64_t mbs = p->cfg.microbatches, mb = p->cfg.microbatch;
+  uint64_t want = env_fuse == 1 || env_fuse == 2 || env_fuse == 4 ? (uint64_t)env_fuse : kFuseDefault;
+  while (want > 1 && mbs % want != 0) want /= 2;
+  if (!p->train_mode || p->world != 1) want = 1;
+  if (want > 1) {
+    // Each group product keeps the one-microbatch product's split count and orientation, so
+    // every element is computed by the same operations in the same order.
+    p->fwd_shape.assign(p->count, {});
+    p->dgrad_shape.assign(p->count, {});
+    for (uint64_t l = 0; l < p->count; l++) {
+      lc_pipeline::Shape& f = p->fwd_shape[l];
+      lc_status st = gemm_plan_shape(p->ctx, fwd_problem(p, l, 0, mb), &f.bn, &f.splits, &f.swap);
+      if (st) return st;
+      if (l > 0) {
+        lc_pipeline::Shape& d = p->dgrad_shape[l];
+        st = gemm_plan_shape(p->ctx, dgrad_problem(p, l, 0, mb, p->dP[l - 1]), &d.bn, &d.splits, &d.swap);
+        if (st) return st;
+      }
+      // A wider tile covers the group's rows (up to 128), so each weight tile is read by one CTA
+      // (pair) for two microbatches; with 64-wide tiles each CTA also re-reads its slice of the
+      // activations, which made the per-SM load, not the DRAM, the limit.
+      if (!env_narrow)
+        for (lc_pipeline::Shape* sh : {&p->fwd_shape[l], &p->dgrad_shape[l]})
+          if (sh->bn == 64 && sh->swap > 0) sh->bn = (int32_t)std::min<uint64_t>(128, 64 * want);
+    }
+  }
+  p->fuse = want;
+  return LC_OK;
+}
+
+// `g` over a group of microbatches, planned from the one-microbatch product's shape
+GemmProblem shaped(GemmProblem g, const lc_pipeline::Shape& sh) {
+  g.bn_hint = sh.bn;
+  g.splits_hint = sh.splits;
+  g.swap_hint = sh.swap;
+  return g;
 }
 
 // W_l -= lr * H[l]^T @ dP[l] (K = B), Wb_l = bf16(W_l); or dW_l = H[l]^T @ dP[l] when lr == 0
@@ -756,10 +819,24 @@ lc_status lc_pipeline_step(lc_pipeline* p, const float* x, const float* target_o
   if (p->is_last() && target_or_dy == nullptr) return fail(LC_ERR_INVALID_ARGUMENT, "the last rank needs targets or dy");
   cudaSetDevice(p->device);
   const uint64_t mbs = p->cfg.microbatches, mb = p->cfg.microbatch;
+  if (p->fuse == 0) {
+    const lc_status fs = decide_fuse(p);
+    if (fs) return fs;
+  }
+  const uint64_t fuse = p->fuse;
   std::vector<int64_t> order(2 * mbs);
   uint64_t n_ops = 0;
-  lc_status st = lc_local_order((uint64_t)p->world, (uint64_t)p->rank, mbs, order.data(), order.size(), &n_ops);
-  if (st) return st;
+  lc_status st = LC_OK;
+  if (fuse > 1) {
+    // one stage: 1F1B is F(m) B(m) in microbatch order; each op here covers `fuse` microbatches
+    for (uint64_t g = 0; g < mbs / fuse; g++) {
+      order[n_ops++] = (int64_t)(g * fuse) + 1;
+      order[n_ops++] = -((int64_t)(g * fuse) + 1);
+    }
+  } else {
+    st = lc_local_order((uint64_t)p->world, (uint64_t)p->rank, mbs, order.data(), order.size(), &n_ops);
+    if (st) return st;
+  }
   cudaStream_t cs = p->comp();
   const ncclDataType_t nt = p->train_mode ? ncclBfloat16 : ncclFloat32;
   const uint64_t w0 = p->win(0), wl = p->wout(p->count - 1);
@@ -779,12 +856,13 @@ lc_status lc_pipeline_step(lc_pipeline* p, const float* x, const float* target_o
     const bool fwd = order[i] > 0;
     const uint64_t m = (uint64_t)(fwd ? order[i] : -order[i]) - 1;
     const uint64_t row0 = m * mb;
+    const uint64_t rows = fuse * mb;  // this op's microbatches m .. m+fuse-1 are adjacent rows
     if (fwd) {
-      const cudaStream_t fs = p->fwd_stream(m);
+      const cudaStream_t fs = p->fwd_stream(m / fuse);
       void* in = (uint8_t*)p->H[0] + row0 * w0 * es;
       if (p->is_first()) {
         if (p->train_mode) {
-          to_bf16_kernel<<<blocks_for(p->ctx, mb * w0), 256, 0, fs>>>(p->x_dev + row0 * w0, (uint16_t*)in, mb * w0);
+          to_bf16_kernel<<<blocks_for(p->ctx, rows * w0), 256, 0, fs>>>(p->x_dev + row0 * w0, (uint16_t*)in, rows * w0);
           record_launch(p->ctx, "pipeline_input_to_bf16");
         } else {
           CU(cudaMemcpyAsync(in, p->x_dev + row0 * w0, mb * w0 * 4, cudaMemcpyDeviceToDevice, fs));
@@ -796,7 +874,8 @@ lc_status lc_pipeline_step(lc_pipeline* p, const float* x, const float* target_o
       }
       if (p->train_mode) {
         std::vector<GemmProblem> probs;
-        for (uint64_t l = 0; l < p->count; l++) probs.push_back(fwd_problem(p, l, row0, mb));
+        for (uint64_t l = 0; l < p->count; l++)
+          probs.push_back(fuse > 1 ? shaped(fwd_problem(p, l, row0, rows), p->fwd_shape[l]) : fwd_problem(p, l, row0, mb));
         st = run_products(p, fs, probs);
       } else {
         for (uint64_t l = 0; l < p->count && !st; l++) st = ref_forward(p, l, row0, mb);
@@ -808,16 +887,20 @@ lc_status lc_pipeline_step(lc_pipeline* p, const float* x, const float* target_o
         CU(cudaStreamWaitEvent(p->s_fwd, p->ev_fd[m], 0));
         NC(nccl().Send(outp, mb * wl, nt, p->rank + 1, p->comm_fwd, p->s_fwd));
       } else if (p->train_mode) {
-        mse_relu_kernel<<<kMseBlocks, kMseThreads, 0, fs>>>((const uint16_t*)outp, p->t_dev + row0 * wl,
-                                                          (uint16_t*)p->dP[p->count - 1] + row0 * wl, mb * wl, n_total,
-                                                          p->part + m * kMseBlocks);
-        record_launch(p->ctx, "pipeline_mse_relu");
+        // one launch per microbatch: its loss partials are summed exactly as without grouping
+        for (uint64_t j = 0; j < fuse; j++) {
+          const uint64_t r = row0 + j * mb;
+          mse_relu_kernel<<<kMseBlocks, kMseThreads, 0, fs>>>((const uint16_t*)p->H[p->count] + r * wl, p->t_dev + r * wl,
+                                                            (uint16_t*)p->dP[p->count - 1] + r * wl, mb * wl, n_total,
+                                                            p->part + (m + j) * kMseBlocks);
+          record_launch(p->ctx, "pipeline_mse_relu");
+        }
       }
       CU(cudaEventRecord(p->ev_fdone[m], fs));
     } else {
       // backward of microbatch m on its own stream, after its forward (activations, masks, the
       // loss gradient) is complete
-      const cudaStream_t bs = p->back_stream(m);
+      const cudaStream_t bs = p->back_stream(m / fuse);
       CU(cudaStreamWaitEvent(bs, p->ev_fdone[m], 0));
       // incoming gradient for the stage's last layer
       const float* g_ref = nullptr;
@@ -833,7 +916,8 @@ lc_status lc_pipeline_step(lc_pipeline* p, const float* x, const float* target_o
       if (p->train_mode) {
         std::vector<GemmProblem> probs;
         for (uint64_t l = p->count; l-- > 0;) {
-          if (l > 0) probs.push_back(dgrad_problem(p, l, row0, mb, p->dP[l - 1]));
+          if (l > 0 && fuse > 1) probs.push_back(shaped(dgrad_problem(p, l, row0, rows, p->dP[l - 1]), p->dgrad_shape[l]));
+          else if (l > 0) probs.push_back(dgrad_problem(p, l, row0, mb, p->dP[l - 1]));
           else if (!p->is_first()) probs.push_back(dgrad_problem(p, 0, row0, mb, p->gsend));
         }
         st = run_products(p, bs, probs);

@@ -161,3 +161,33 @@ def test_weight_update_on_two_sm_tiles(gpu, tmp_path):
         step = np.abs(a[f"w{l}"] - a[f"w0_{l}"]).max()
         assert step > 0
         assert np.abs(a[f"w{l}"] - b[f"w{l}"]).max() <= 1e-3 * step, l
+
+
+@pytest.mark.parametrize("width", [1024, 8192])
+def test_grouped_microbatches_equal_one_at_a_time(gpu, tmp_path, width):
+    """On one stage, consecutive microbatches run as one product per layer (four by default,
+    two with LC_PIPE_FUSE=2), so one pass over each weight matrix serves the group.  Each group
+    product keeps the one-microbatch product's split count and orientation, so the losses and
+    the updated weights equal those of one microbatch at a time (LC_PIPE_FUSE=1) bit for bit.
+    Width 1024 runs the products split-K; width 8192 on CTA pairs."""
+    import os
+    import subprocess
+    import sys
+    here = Path(__file__).resolve().parent
+    cfg = {"layers": 3 if width == 1024 else 2, "width": width, "microbatch": 64, "microbatches": 8, "lr": 1e-2,
+           "steps": 2, "seed": 11, "rank": 0, "world": 1, "uid": ""}
+    outs = {}
+    for fuse in ("1", "2", "4"):
+        env = dict(os.environ, LC_PIPE_FUSE=fuse)
+        c = dict(cfg, out=str(tmp_path / f"f{fuse}.npz"))
+        r = subprocess.run([sys.executable, str(here / "_pipeline_rank.py"), json.dumps(c)], env=env,
+                           capture_output=True, text=True, timeout=600)
+        assert r.returncode == 0, r.stdout + r.stderr
+        outs[fuse] = np.load(tmp_path / f"f{fuse}.npz")
+    one = outs["1"]
+    assert one["losses"][1] < one["losses"][0]
+    for fuse in ("2", "4"):
+        got = outs[fuse]
+        assert got["losses"].tobytes() == one["losses"].tobytes(), fuse
+        for l in range(cfg["layers"]):
+            assert got[f"w{l}"].tobytes() == one[f"w{l}"].tobytes(), (fuse, l)
