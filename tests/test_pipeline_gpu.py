@@ -111,7 +111,9 @@ def test_training_step_is_deterministic(gpu):
 def test_layer_chains_equal_one_launch_per_layer(gpu, tmp_path):
     """Each microbatch's layer loop runs as one chain launch (CTAs resident across layers);
     the products and their order of summation are those of one launch per layer, so the
-    losses and weights match bit for bit (LC_GEMM_CHAIN=0 forces one launch per layer)."""
+    losses and weights match bit for bit (LC_GEMM_CHAIN=0 forces one launch per layer).  One
+    microbatch per product (LC_PIPE_FUSE=1), as every stage of a multi-GPU run computes them:
+    one-stage microbatch groups run as one launch per layer, not as chains."""
     import os
     import subprocess
     import sys
@@ -120,7 +122,7 @@ def test_layer_chains_equal_one_launch_per_layer(gpu, tmp_path):
            "rank": 0, "world": 1, "uid": ""}
     outs = {}
     for mode in ("chain", "layers"):
-        env = dict(os.environ)
+        env = dict(os.environ, LC_PIPE_FUSE="1")
         if mode == "layers":
             env["LC_GEMM_CHAIN"] = "0"
         c = dict(cfg, out=str(tmp_path / f"{mode}.npz"))
