@@ -75,9 +75,9 @@ lc_status gemm_run(lc_context* ctx, cudaStream_t s, const GemmProblem& p, lc_con
 // `max_clusters` (> 0) caps the CTA pairs, leaving the rest of the SMs to work on another
 // stream (each pair then takes several tiles of a product).
 // The tile width, split count and orientation gemm_run would choose for `pr` (no launch, no
-// allocation), the orientation as 1 (C^T = B^T A^T) or -1.  Products over more rows that keep
-// the split count and orientation compute every output element with the same operations in the
-// same order (the tile width does not enter an element's arithmetic).
+// allocation), the orientation as 1 (C^T = B^T A^T) or -1.  A product over more rows that keeps
+// the split count and orientation keeps every output element's k order, split and pair sum; the
+// pipeline's grouping test finds the results bit-equal with 64- and 128-wide tiles.
 lc_status gemm_plan_shape(lc_context* ctx, const GemmProblem& pr, int32_t* bn, int32_t* splits, int32_t* swap);
 
 lc_status gemm_chain_run(lc_context* ctx, cudaStream_t s, const GemmProblem* probs, int n, bool a_stable,
