@@ -6,7 +6,7 @@ contraction and bandwidth-op figures at N = 1.
 
 Under torchrun (N > 1) every rank builds one stage; rank 0 prints one JSON line.
 
-Workload: 32 x Linear 8192->8192 + ReLU, bf16 compute weights with f32
+Workload (the reference's pipeline benchmark configuration): 32 x Linear 8192->8192 + ReLU, bf16 compute weights with f32
 masters initialised N(0, 1/8192), global batch 2048 = 32 microbatches x 64 rows, synthetic
 N(0, 1) inputs and targets (seeded SplitMix64), MSE loss, SGD lr 1e-3; layers split evenly by
 contiguous placement across the N stages.
@@ -15,7 +15,9 @@ contiguous placement across the N stages.
 stream, barrier + synchronize on both sides, max over ranks).  `e2e` times K more steps through
 the same public call with the inputs in pinned host memory: every step copies its inputs to the
 device and its loss back.  `--impl reference` times the reference's CPU path (the C oracle
-restating crates/cpu's gemm, all host threads) on a bounded sample of the same workload.
+restating crates/cpu's gemm, on every host thread) on a bounded sample of the same workload and
+extrapolates it to the step; it also times one whole training step of the oracle on a reduced
+configuration, and says so.
 """
 from __future__ import annotations
 
@@ -28,12 +30,15 @@ import sys
 import time
 from pathlib import Path
 
+import numpy as np
+
 ROOT = Path(__file__).resolve().parent
 sys.path.insert(0, str(ROOT))
 sys.path.insert(0, str(ROOT / "pipeline-parallelism-deep-learning-library_b200"))
 
 LAYERS, WIDTH, MB, MBS, LR = 32, 8192, 64, 32, 1e-3
 BATCH = MB * MBS
+STEP_FLOP = 6 * BATCH * WIDTH * WIDTH * LAYERS
 METRIC = "1F1B MLP training samples/s (32 x 8192 Linear+ReLU, bf16, batch 2048 = 32 x 64)"
 WORKLOAD = "1F1B MLP training step: 32 x Linear 8192->8192 + ReLU, bf16 weights / f32 master, " \
            "global batch 2048 = 32 microbatches x 64, MSE, SGD lr 1e-3"
@@ -44,11 +49,13 @@ def env_rank():
 
 
 def peaks():
+    """(HBM GB/s, bf16 TFLOP/s burst, bf16 TFLOP/s sustained, kind) measured on this pool."""
     p = ROOT / "MEASURED_PEAKS.json"
     if p.exists():
         d = json.loads(p.read_text())
-        return float(d["hbm_gbs"]), float(d["bf16_tflops"]), "measured"
-    return 6650.0, 1590.0, "fallback"
+        return (float(d["hbm_gbs"]), float(d["bf16_tflops"]),
+                float(d.get("bf16_tflops_sustained", d["bf16_tflops"])), "measured")
+    return 6650.0, 1590.0, 1400.0, "fallback"
 
 
 class Clocks:
@@ -124,6 +131,28 @@ def cpu_sample(threads: int):
     return BATCH / step_s, dt
 
 
+def config_dict(world: int) -> dict:
+    """The workload, identical in both arms' lines."""
+    return {"workload": WORKLOAD, "layers": LAYERS, "width": WIDTH, "global_batch": BATCH, "microbatch": MB,
+            "microbatches": MBS, "stages": world, "parallelism": f"pp{world}",
+            "l2": "inputs larger than L2: every GEMM streams a 128 MiB weight matrix from HBM"}
+
+
+def reduced_step_seconds():
+    """One whole training step of the oracle (crates/cpu's gemm and training ops, the sequential
+    pipeline reference) on a reduced configuration: d = 512, 4 layers, 8 microbatches of 16."""
+    from linalg_b200 import data
+    from oracle import oracle as O
+
+    L, d, mbs, mb = 4, 512, 8, 16
+    master = np.stack([data.normal(100 + l, (d, d), scale=d ** -0.5) for l in range(L)])
+    x = data.normal(1, (mbs * mb, d))
+    t = data.normal(2, (mbs * mb, d))
+    t0 = time.perf_counter()
+    O.mlp_step(master, x, t, mb, LR)
+    return time.perf_counter() - t0, {"layers": L, "width": d, "microbatches": mbs, "microbatch": mb}
+
+
 def run_reference(args):
     rank, world, _ = env_rank()
     if rank != 0:
@@ -137,16 +166,23 @@ def run_reference(args):
         vals.append(v)
         secs.append(s)
     value = statistics.median(vals)
+    red_s, red_cfg = reduced_step_seconds()
+    sample = (f"one microbatch x one layer ([64,8192]x[8192,8192] bf16, f32 k-order accumulate) per step on "
+              f"{threads} threads, median {statistics.median(secs):.3f} s, scaled by 3 products x 32 layers x "
+              f"32 microbatches (activation, loss and SGD work not counted); the Rust reference cannot be "
+              f"built here, the C oracle restates crates/cpu")
     line = {
         "impl": "reference", "metric": METRIC, "value": value, "unit": "samples/s", "n_gpus": args.gpus,
         "steps": args.steps, "warmup": args.warmup, "ms_per_step": 1000.0 * BATCH / value, "higher_is_better": True,
-        "scaling": "strong", "vs_baseline": None, "dtype": "bf16 in, f32 accumulate", "data": "synthetic",
-        "config": {"workload": WORKLOAD, "layers": LAYERS, "width": WIDTH, "global_batch": BATCH,
-                   "microbatch": MB, "microbatches": MBS, "parallelism": f"pp{args.gpus}"},
-        "cpu_baseline": {"value": value, "unit": "samples/s", "cores": threads, "kind": "port",
-                         "sample": f"one microbatch x one layer ([64,8192]x[8192,8192]) per step, "
-                                   f"median {statistics.median(secs):.2f} s, scaled by 3 x 32 layers x 32 microbatches; "
-                                   f"the Rust reference cannot be built here, the C oracle restates crates/cpu"},
+        "scaling": "strong", "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
+        "config": config_dict(world),
+        "extrapolated": True,
+        "sampled_seconds_per_step": statistics.median(secs),
+        "timed_seconds": sum(secs),
+        "cpu_baseline": {"value": value, "unit": "samples/s", "cores": threads, "kind": "port", "sample": sample},
+        "reduced_step": {"config": red_cfg, "seconds": red_s, "samples_per_s": red_cfg["microbatches"] *
+                         red_cfg["microbatch"] / red_s, "threads": 1,
+                         "what": "one whole training step of the CPU oracle, measured, not extrapolated"},
         "e2e": {"value": value, "unit": "samples/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }
     print(json.dumps(line), flush=True)
@@ -245,40 +281,54 @@ def op_figures(hbm_peak, tc_peak):
     return out
 
 
-# dram__bytes_read.sum + dram__bytes_write.sum of one launch of the forward product, from the ncu
-# capture summarised in profiles/gemm_bf16_pair_n64_fwd_64x8192x8192.md (135.37 MB + 4.77 MB)
+# dram__bytes_read.sum + dram__bytes_write.sum of one launch, from the ncu captures of the
+# profiling drivers below (`--profile group` and `--profile gemm`); None until captured
+TRAFFIC_GROUP_GEMM = None
 TRAFFIC_FWD_GEMM = 140_140_544
 
 
-def forward_gemm_roofline(hbm_peak):
-    """The step's dominant kernel: the forward/dgrad GEMM [64, 8192] x [8192, 8192] bf16 that
-    streams one weight matrix from HBM.  Timed alone with CUDA events on its launch stream."""
+def product_roofline(hbm_peak, tc_peak, rows: int, grouped: bool):
+    """One forward product of the step, timed alone with CUDA events on its launch stream over 4
+    rotating weight matrices (512 MiB, 4x L2, so every launch streams its weights from HBM).
+    grouped: the one-stage step's product over four microbatches, [256, 8192] x [8192, 8192] with
+    the fused ReLU, pinned as the pipeline pins it (2-way split over a CTA pair, C^T = W^T H^T,
+    256-wide tile); otherwise one microbatch [64, 8192] x [8192, 8192], the product every stage of
+    a multi-GPU run streams.  Algorithmic bytes: the weights once plus activations in and out."""
     import torch
     import linalg_b200 as lb
 
     ctx = lb.Context(torch.cuda.current_device())
     st = ctx.stream
-    # 4 distinct weight matrices (512 MiB, 4x L2) so no launch finds its weights in L2
     ws = [torch.randn(WIDTH, WIDTH, device="cuda").bfloat16() for _ in range(4)]
-    x = torch.randn(MB, WIDTH, device="cuda").bfloat16()
-    y = torch.empty(MB, WIDTH, device="cuda", dtype=torch.bfloat16)
+    x = torch.randn(rows, WIDTH, device="cuda").bfloat16()
+    y = torch.empty(rows, WIDTH, device="cuda", dtype=torch.bfloat16)
     i = [0]
+    pin = dict(tile_n=256, splits=2, swap=1) if grouped else {}
 
     def one():
-        lb.encode_gemm(ctx, st, 1.0, x, ws[i[0] % 4], 0.0, y)
+        lb.encode_gemm_fused(ctx, st, 1.0, x, ws[i[0] % 4], 0.0, y, lb.EPI_RELU, **pin)
         i[0] += 1
 
     ms = time_launches(one, st, 64)
-    algo_bytes = WIDTH * WIDTH * 2 + 2 * MB * WIDTH * 2
-    achieved = algo_bytes / (ms * 1e-3) / 1e9
+    name = ctx.debug_launches()[-1]
+    algo_bytes = WIDTH * WIDTH * 2 + 2 * rows * WIDTH * 2
+    flops = 2 * rows * WIDTH * WIDTH
     del ws, x, y
     ctx.close()
     torch.cuda.empty_cache()
-    return {"bound": "hbm", "achieved": achieved, "peak": hbm_peak, "unit": "GB/s", "frac": achieved / hbm_peak,
-            "traffic": TRAFFIC_FWD_GEMM,
-            "kernel": "gemm_tc_kernel<BN=64, bf16, pair> (K split over a CTA pair, reduced through distributed "
-                      "shared memory), forward/dgrad shape [64,8192]x[8192,8192]",
-            "algorithmic_bytes_per_launch": algo_bytes, "ms_per_launch": ms}
+    t_hbm = algo_bytes / (hbm_peak * 1e9)
+    t_tc = flops / (tc_peak * 1e12)
+    gbs = algo_bytes / (ms * 1e-3) / 1e9
+    tfs = flops / (ms * 1e-3) / 1e12
+    out = {"kernel": name, "rows": rows, "algorithmic_bytes_per_launch": algo_bytes, "flop_per_launch": flops,
+           "ms_per_launch": ms, "gbs": gbs, "tflops": tfs,
+           "frac_of_roofline": max(t_hbm, t_tc) / (ms * 1e-3)}
+    if t_hbm >= t_tc:
+        out.update({"bound": "hbm", "achieved": gbs, "peak": hbm_peak, "unit": "GB/s", "frac": gbs / hbm_peak})
+    else:
+        out.update({"bound": "tensor", "achieved": tfs, "peak": tc_peak, "unit": "TFLOP/s", "frac": tfs / tc_peak})
+    out["traffic"] = TRAFFIC_GROUP_GEMM if grouped else TRAFFIC_FWD_GEMM
+    return out
 
 
 def run_profile(args):
@@ -289,15 +339,19 @@ def run_profile(args):
     from linalg_b200.pipeline import Pipeline
 
     torch.cuda.set_device(0)
-    if args.profile == "gemm":
+    if args.profile in ("gemm", "group"):
+        # --steps forward products as product_roofline times them: one microbatch ('gemm') or the
+        # one-stage step's group of four ('group'), fused ReLU, 4 rotating weight matrices
         ctx = lb.Context(0)
+        rows = MB if args.profile == "gemm" else 4 * MB
+        pin = dict(tile_n=256, splits=2, swap=1) if args.profile == "group" else {}
         ws = [torch.randn(WIDTH, WIDTH, device="cuda").bfloat16() for _ in range(4)]
-        x = torch.randn(MB, WIDTH, device="cuda").bfloat16()
-        y = torch.empty(MB, WIDTH, device="cuda", dtype=torch.bfloat16)
+        x = torch.randn(rows, WIDTH, device="cuda").bfloat16()
+        y = torch.empty(rows, WIDTH, device="cuda", dtype=torch.bfloat16)
         for i in range(args.steps):
-            lb.encode_gemm(ctx, None, 1.0, x, ws[i % 4], 0.0, y)
+            lb.encode_gemm_fused(ctx, None, 1.0, x, ws[i % 4], 0.0, y, lb.EPI_RELU, **pin)
         ctx.sync()
-        print(json.dumps({"profile": "gemm", "launches": ctx.debug_launches()[-8:]}))
+        print(json.dumps({"profile": args.profile, "launches": ctx.debug_launches()[-8:]}))
         return 0
     if args.profile == "square":
         # --warmup + --steps back-to-back 8192^3 bf16 products (the gemm_bf16_8192 figure)
@@ -361,9 +415,10 @@ def main():
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--no-extras", action="store_true", help="skip the N=1 contraction/op figures")
     ap.add_argument("--layers", type=int, default=LAYERS, help="profiling driver only: pipeline depth")
-    ap.add_argument("--profile", choices=["step", "gemm", "ops", "square"], default=None,
+    ap.add_argument("--profile", choices=["step", "gemm", "group", "ops", "square"], default=None,
                     help="profiling driver: 'step' runs --warmup + --steps pipeline steps and nothing else; "
                          "'gemm' runs --steps forward-shaped GEMMs ([64,8192] x [8192,8192] bf16); "
+                         "'group' runs --steps grouped forward products ([256,8192] x [8192,8192]); "
                          "'ops' runs --warmup + --steps rounds of the op-figure configs (pack, bf16 and "
                          "f32 split-K, argmax rows, permute, sqrt); 'square' runs --warmup + --steps "
                          "8192^3 bf16 products")
@@ -387,13 +442,16 @@ def main():
     from linalg_b200 import data
     from linalg_b200.pipeline import Pipeline, unique_id
 
-    hbm_peak, tc_peak, peak_kind = peaks()
+    hbm_peak, tc_peak, tc_sustained, peak_kind = peaks()
     extras = None
     roof = None
     if rank == 0 and world == 1 and not args.no_extras:
         extras = op_figures(hbm_peak, tc_peak)
+    roof_one = None
     if rank == 0:
-        roof = forward_gemm_roofline(hbm_peak)
+        # the dominant kernel: the grouped product on one stage, the one-microbatch product on several
+        roof_one = product_roofline(hbm_peak, tc_peak, MB, grouped=False)
+        roof = product_roofline(hbm_peak, tc_peak, 4 * MB, grouped=True) if world == 1 else roof_one
 
     uid = None
     if world > 1:
@@ -465,17 +523,22 @@ def main():
             "warmup": args.warmup, "ms_per_step": ms / args.steps, "higher_is_better": True, "scaling": "strong",
             "vs_baseline": None, "dtype": "bf16", "data": "synthetic (seeded SplitMix64 N(0,1) inputs/targets, "
                                                           "N(0,1/8192) weights on device)",
-            "config": {"workload": WORKLOAD, "layers": LAYERS, "width": WIDTH, "global_batch": BATCH,
-                       "microbatch": MB, "microbatches": MBS, "stages": world, "parallelism": f"pp{world}",
-                       "l2": "inputs larger than L2: every GEMM streams a 128 MiB weight matrix from HBM"},
+            "config": config_dict(world),
             "e2e": {"value": e2e, "unit": "samples/s", "h2d_bytes_per_step": (BATCH * WIDTH * 4) * 2,
                     "d2h_bytes_per_step": 4},
             "gpu_launches": launches,
             "clocks": clocks,
             "loss": final_loss,
             "roofline": roof,
-            "peaks": {"kind": peak_kind, "hbm_gbs": hbm_peak, "bf16_tflops": tc_peak},
+            "peaks": {"kind": peak_kind, "hbm_gbs": hbm_peak, "bf16_tflops": tc_peak,
+                      "bf16_tflops_sustained": tc_sustained},
+            # 6 B d^2 L flop per step (forward, data and weight gradients) against the sustained
+            # bf16 peak: the whole step, inside which every kernel runs under the power cap
+            "step_tflops": STEP_FLOP / (ms / args.steps * 1e-3) / 1e12,
+            "step_frac_of_sustained_bf16": STEP_FLOP / (ms / args.steps * 1e-3) / 1e12 / tc_sustained,
         }
+        if world == 1:
+            line["roofline_one_microbatch"] = roof_one
         if cpu_v is not None:
             line["cpu_baseline"] = {"value": cpu_v, "unit": "samples/s", "cores": 1, "kind": "port",
                                     "sample": f"one microbatch x one layer bf16 product ({cpu_s:.2f} s, 1 thread), "

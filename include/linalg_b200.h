@@ -132,6 +132,36 @@ lc_status lc_encode_gemm(lc_context* ctx, void* stream, float alpha, const lc_vi
                          float beta, const lc_view* c);
 lc_status lc_gemm(lc_context* ctx, float alpha, const lc_view* a, const lc_view* b, float beta,
                   const lc_view* c);
+/* Fused epilogues: the training step's elementwise op applied by the product's own epilogue
+ * warps, instead of a Backend::gemm followed by a separate training op (crates/core/src/lib.rs:
+ * 166-236, the ops crates/pipeline/src/lib.rs:176-221 calls after each gemm; crates/cuda/train.cu
+ * and gelu.cu are the reference's standalone kernels).  Every kind gives the bits of the unfused
+ * sequence: the product rounded to f32 as lc_encode_gemm would store it, then the op.  `aux` and
+ * `aux2` are views with C's shape, strides and offset. */
+typedef enum lc_epilogue_kind {
+    LC_EPI_NONE = 0,       /* C = alpha*A*B + beta*C (lc_encode_gemm) */
+    LC_EPI_RELU = 1,       /* C = relu(alpha*A*B + beta*C): a ReLU layer's forward (the benchmark's
+                              layers; the reference's own layers use `gelu`, :169) */
+    LC_EPI_RELU_MASK = 2,  /* C = alpha*A*B where aux > 0, else +0; aux bf16 (16-bit inputs): the
+                              data gradient through the ReLU of the layer whose input aux is
+                              (lc_relu_backward's rule) */
+    LC_EPI_SGD = 3,        /* C (f32 master weights) = C - lr*(alpha*A*B); aux2 (bf16) = bf16(C)
+                              (16-bit inputs; beta unused): the weight gradient with `sgd_step`
+                              and `convert` fused (crates/cpu/src/lib.rs:474-533) */
+} lc_epilogue_kind;
+typedef struct lc_epilogue {
+    int32_t kind;          /* lc_epilogue_kind */
+    const lc_view* aux;
+    const lc_view* aux2;
+    float lr;
+    /* plan hints, 0 = the planner's choice (the pipeline pins its grouped products with them) */
+    int32_t tile_n;        /* kernel tile width 64, 128 or 256 (16-bit inputs) */
+    int32_t splits;        /* split-K slices */
+    int32_t swap;          /* 1: compute C^T = B^T A^T; -1: never */
+} lc_epilogue;
+lc_status lc_encode_gemm_fused(lc_context* ctx, void* stream, float alpha, const lc_view* a,
+                               const lc_view* b, float beta, const lc_view* c,
+                               const lc_epilogue* epi);
 /* lc_encode_gemm that allocates no device memory (no counterpart in the reference, whose
  * backends allocate per call).  For callers that must not allocate while they run: a process
  * that reserves the card's memory up front, where a pool grown mid-step can run out, or a

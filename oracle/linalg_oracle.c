@@ -21,7 +21,8 @@
 #include <string.h>
 
 #if defined(__FP_FAST_FMAF) && !defined(LINALG_ORACLE_ALLOW_FMA)
-/* -ffp-contract=off keeps the compiler from fusing; an explicit fmaf is never called. */
+/* -ffp-contract=off keeps the compiler from fusing; an explicit fmaf appears only where the
+ * reference itself calls `mul_add` (or_mag32). */
 #endif
 
 static inline uint32_t f2u(float f) { uint32_t u; memcpy(&u, &f, 4); return u; }
@@ -318,6 +319,33 @@ void or_argmax_rows(const float* x, uint64_t rows, uint64_t cols, uint64_t row_s
     for (uint64_t r = 0; r < rows; r++) out[r] = (uint32_t)or_argmax(x + r * row_stride, cols, col_stride);
 }
 
+/* Complex magnitude in f32: tests/argmax_test.rs:51-72 (`mag32`).  kind 0 = L1 (|re| + |im|),
+ * kind 1 = Hypot (hi * sqrt(fma(r, r, 1)) with r = lo / hi, so nothing overflows near f32 max).
+ * A NaN part gives NaN; subnormals take part (no flush to zero). */
+float or_mag32(float re_in, float im_in, int kind) {
+    float re = fabsf(re_in), im = fabsf(im_in);
+    if (isnan(re) || isnan(im)) return NAN;
+    if (kind == 0) return re + im;
+    float hi = re > im ? re : im, lo = re > im ? im : re;
+    if (hi == 0.0f) return 0.0f;
+    if (isinf(hi)) return INFINITY;
+    float r = lo / hi;
+    return hi * sqrtf(fmaf(r, r, 1.0f));
+}
+
+/* `ref_argmax_complex` (tests/argmax_test.rs:74-76): `ref_best` over the f32 magnitudes of n
+ * complex values (interleaved re, im) at a stride of `stride` complex elements. */
+uint64_t or_argmax_complex(const float* z, uint64_t n, uint64_t stride, int kind) {
+    float bm = 0.0f;
+    uint64_t bi = 0;
+    int have = 0;
+    for (uint64_t i = 0; i < n; i++) {
+        float m = or_mag32(z[2 * i * stride], z[2 * i * stride + 1], kind);
+        if (!have || or_beats(m, i, bm, bi)) { bm = m; bi = i; have = 1; }
+    }
+    return bi;
+}
+
 /* ------------------------------------------------------------------------------------ */
 /* sqrt: tests/sqrt_test.rs:25-27 `reference(x) = (x as f64).sqrt() as f32`.             */
 /* reciprocal: tests/reciprocal_test.rs:137-140 `reference_real(x) = (1.0 / x as f64) as f32`. */
@@ -496,7 +524,7 @@ void or_sgd_step(float* w, float* dw, uint64_t count, float lr) {
     }
 }
 
-/* ReLU is absent from the reference (the BASELINE pipeline asks for it).  Stated as
+/* ReLU is absent from the reference (the benchmark's MLP layers use it).  Stated as
  * `x > 0 ? x : +0`: -0, NaN and negatives give +0.  relu'(pre) selects dy where pre > 0.
  * The GPU kernels evaluate the same expression. */
 void or_relu(const float* x, float* y, uint64_t n) {

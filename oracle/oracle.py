@@ -59,6 +59,8 @@ def lib() -> C.CDLL:
             "or_scatter": (None, [_ptr, _u64, _ptr, _u64, C.c_int, _ptr, _ptr]),
             "or_argmax": (_u64, [_ptr, _u64, _u64]),
             "or_argmax_rows": (None, [_ptr, _u64, _u64, _u64, _u64, _ptr]),
+            "or_mag32": (_f32, [_f32, _f32, C.c_int]),
+            "or_argmax_complex": (_u64, [_ptr, _u64, _u64, C.c_int]),
             "or_sqrt": (None, [_ptr, _ptr, _u64]),
             "or_reciprocal": (None, [_ptr, _ptr, _u64]),
             "or_reciprocal_c32": (None, [_ptr, _ptr, _u64]),
@@ -265,6 +267,24 @@ def argmax(x: np.ndarray, stride: int = 1, n: int | None = None) -> int:
     x = np.ascontiguousarray(x, dtype=np.float32)
     n = x.size if n is None else n
     return int(lib().or_argmax(_p(x), n, stride))
+
+
+MAG_L1, MAG_HYPOT = 0, 1
+
+
+def mag32(re: float, im: float, kind: int) -> float:
+    """tests/argmax_test.rs:51-72 `mag32`: the f32 complex magnitude the kernel ranks by."""
+    return float(lib().or_mag32(float(np.float32(re)), float(np.float32(im)), kind))
+
+
+def argmax_complex(z: np.ndarray, kind: int, stride: int = 1, n: int | None = None) -> int:
+    """tests/argmax_test.rs:74-76 `ref_argmax_complex`; z is complex64 (or float32 pairs)."""
+    z = np.ascontiguousarray(z)
+    if z.dtype == np.complex64:
+        z = z.view(np.float32)
+    z = np.ascontiguousarray(z, dtype=np.float32).reshape(-1)
+    n = z.size // 2 if n is None else n
+    return int(lib().or_argmax_complex(_p(z), n, stride, kind))
 
 
 def argmax_rows(x: np.ndarray) -> np.ndarray:

@@ -564,6 +564,78 @@ lc_status gemm_impl(lc_context* ctx, void* stream, float alpha, const lc_view* a
   return execute(ctx, stream_of(ctx, stream), plan, nullptr, false);
 }
 
+// A fused epilogue's side view must be laid out exactly like C: the epilogue reads and writes it
+// at C's element index.
+lc_status same_layout_as_c(const lc_view* v, const lc_view& c, int32_t dtype, const char* what) {
+  if (v == nullptr) return fail(LC_ERR_INVALID_ARGUMENT, std::string("this epilogue needs ") + what);
+  lc_status st = validate(*v, what);
+  if (st) return st;
+  if (v->dtype != dtype) return fail(LC_ERR_DTYPE, std::string(what) + " has the wrong element type");
+  if (v->rank != c.rank || v->offset != c.offset) return fail(LC_ERR_SHAPE, std::string(what) + " must be laid out like C");
+  for (int i = 0; i < c.rank; i++)
+    if (v->shape[i] != c.shape[i] || (c.shape[i] > 1 && v->strides[i] != c.strides[i]))
+      return fail(LC_ERR_SHAPE, std::string(what) + " must be laid out like C");
+  return LC_OK;
+}
+
+lc_status gemm_fused_impl(lc_context* ctx, void* stream, float alpha, const lc_view* a, const lc_view* b, float beta,
+                          const lc_view* c, const lc_epilogue* e) {
+  if (ctx == nullptr || e == nullptr || c == nullptr) return fail(LC_ERR_INVALID_ARGUMENT, "null argument");
+  // SGD: A and B are 16-bit, C (the master weights) f32; the type checks see a C of the inputs'
+  // type with C's geometry
+  lc_view c16 = *c;
+  if (e->kind == LC_EPI_SGD && a != nullptr) {
+    if (c->dtype != LC_F32) return fail(LC_ERR_DTYPE, "the SGD epilogue updates f32 master weights");
+    lc_status vs = validate(*c, "C");
+    if (vs) return vs;
+    c16.dtype = a->dtype;
+  }
+  lc_status st = prepare(a, b, &c16);
+  if (st) return st;
+  if (e->kind < LC_EPI_NONE || e->kind > LC_EPI_SGD) return fail(LC_ERR_INVALID_ARGUMENT, "unknown epilogue kind");
+  if (e->tile_n != 0 && e->tile_n != 64 && e->tile_n != 128 && e->tile_n != 256)
+    return fail(LC_ERR_INVALID_ARGUMENT, "tile_n is 0, 64, 128 or 256");
+  if (e->splits < 0) return fail(LC_ERR_INVALID_ARGUMENT, "negative split count");
+  const bool sixteen = a->dtype != LC_F32;
+  if ((e->kind == LC_EPI_RELU_MASK || e->kind == LC_EPI_SGD) && !sixteen)
+    return fail(LC_ERR_DTYPE, "the mask and SGD epilogues take bf16 or f16 inputs");
+  Groups g;
+  if ((st = groups_from_gemm(*a, *b, c16, &g))) return st;
+  Plan plan;
+  if ((st = plan_groups(ctx, *a, *b, *c, g, alpha, beta, &plan))) return st;
+  if (e->kind != LC_EPI_NONE) {
+    if (plan.kind != 2) return fail(LC_ERR_INVALID_ARGUMENT, "fused epilogues need alpha != 0 and K > 0");
+    if (plan.stage_c)
+      return fail(LC_ERR_UNSUPPORTED_LAYOUT, "fused epilogues need C with one stride per index group");
+  }
+  GemmProblem& pr = plan.prob;
+  pr.bn_hint = e->tile_n;
+  pr.splits_hint = e->splits;
+  pr.swap_hint = e->swap;
+  switch (e->kind) {
+    case LC_EPI_RELU:
+      pr.relu = 1;
+      break;
+    case LC_EPI_RELU_MASK:
+      if ((st = same_layout_as_c(e->aux, *c, LC_BF16, "aux (the ReLU mask source)"))) return st;
+      pr.epi = 1;
+      pr.aux = e->aux->data;
+      break;
+    case LC_EPI_SGD:
+      if ((st = same_layout_as_c(e->aux2, *c, LC_BF16, "aux2 (the bf16 weight copy)"))) return st;
+      if (e->aux2->data == c->data) return fail(LC_ERR_ALIAS, "aux2 shares C's storage");
+      pr.epi = 2;
+      pr.aux = c->data;
+      pr.aux2 = e->aux2->data;
+      pr.lr = e->lr;
+      pr.c_dtype = LC_F32;
+      break;
+    default:
+      break;
+  }
+  return execute(ctx, stream_of(ctx, stream), plan, nullptr, false);
+}
+
 }  // namespace
 
 namespace lc {
@@ -614,6 +686,11 @@ lc_status lc_plan_contract(lc_context* ctx, float alpha, const lc_view* a, const
 lc_status lc_encode_gemm(lc_context* ctx, void* stream, float alpha, const lc_view* a, const lc_view* b, float beta,
                          const lc_view* c) {
   return gemm_impl(ctx, stream, alpha, a, b, beta, c);
+}
+
+lc_status lc_encode_gemm_fused(lc_context* ctx, void* stream, float alpha, const lc_view* a, const lc_view* b,
+                               float beta, const lc_view* c, const lc_epilogue* epi) {
+  return gemm_fused_impl(ctx, stream, alpha, a, b, beta, c, epi);
 }
 
 lc_status lc_gemm(lc_context* ctx, float alpha, const lc_view* a, const lc_view* b, float beta, const lc_view* c) {

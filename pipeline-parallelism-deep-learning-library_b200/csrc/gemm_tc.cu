@@ -85,8 +85,12 @@ struct Cfg {
   // TWO_SM: each CTA of the pair holds half of the tile's BN rows of B^T
   static constexpr int B_BYTES = (TWO_SM ? BN / 2 : BN) * kRowBytes;
   static constexpr int STAGE_BYTES = (A_BYTES + B_BYTES) * (TF32X3 ? 2 : 1);
-  // PAIR: the peer's raw partial of this CTA's column half lands here (f32, 128 x BN/2)
-  static constexpr int RECV_BYTES = PAIR ? kBM * (BN / 2) * 4 : 0;
+  // PAIR: the peer's raw partial of this CTA's column half lands here (f32, 128 x RECV_COLS), in
+  // EXCH_ROUNDS rounds of RECV_COLS columns (two rounds for BN = 256, so that the ring keeps 4
+  // stages of 48 KiB beside the buffer)
+  static constexpr int RECV_COLS = BN / 2 < 64 ? BN / 2 : 64;
+  static constexpr int EXCH_ROUNDS = (BN / 2) / RECV_COLS;
+  static constexpr int RECV_BYTES = PAIR ? kBM * RECV_COLS * 4 : 0;
   static constexpr int STAGES_FIT = (kSmemMax - 1024 - 512 - RECV_BYTES) / STAGE_BYTES;
   static constexpr int STAGES = PAIR ? (STAGES_FIT < 8 ? STAGES_FIT : 8) : 196608 / STAGE_BYTES;
   // 2 accumulators (+ the 3xTF32 running sum), rounded up to the power of two tcgen05.alloc takes
@@ -108,7 +112,8 @@ struct Cfg {
   static constexpr int SMEM = STAGES * STAGE_BYTES + ((BAR_BYTES + 15) / 16) * 16 + RECV_BYTES + EPI_STAGE_BYTES + 1024;
   static_assert(STAGES >= 2, "at least two stages");
   static_assert(SMEM <= kSmemMax, "shared memory budget");
-  static_assert(!PAIR || (!TF32X3 && BN <= 128), "CTA pairs: 16-bit inputs, BN <= 128");
+  static_assert(!PAIR || (!TF32X3 && BN <= 256), "CTA pairs: 16-bit inputs, BN <= 256");
+  static_assert(!PAIR || STAGES >= 4, "CTA pairs keep at least 4 stages in flight");
   static_assert(!TWO_SM || (!TF32X3 && !PAIR && BN == 256), "2-SM products: 16-bit inputs, BN = 256");
 };
 
@@ -961,6 +966,7 @@ __device__ __forceinline__ void gemm_body(const Src& src) {
     int32_t h = 0;
     bool ok = true;
     uint32_t uo = 0;  // unit ordinal (the converters count the same units)
+    uint32_t xr = 0;  // PAIR: exchange rounds so far (the receive barriers' phase)
     lcd::griddep_wait();
     for (int l = 0; ok && l < src.layers(); l++) {
     decltype(auto) p = src.kp(l);  // a chain's are copied to registers once per product
@@ -1052,11 +1058,13 @@ __device__ __forceinline__ void gemm_body(const Src& src) {
         // the tile: each CTA writes the raw accumulator columns of the other half into the
         // other's receive buffer through distributed shared memory, then adds what it received
         // to its own half in split order (rank 0's partial first, from +0, as the global split-K
-        // paths sum) and runs the epilogue.  Receive buffer: 128 rows x BN/2 floats, 16-byte
-        // chunk c of row r stored at c ^ (r & 7), so the 32 rows a warp touches at once spread
-        // over all banks.
-        constexpr int HB = BN / 2;   // floats per receive-buffer row
-        constexpr int GH = BN / 64;  // 32-column groups per half
+        // paths sum) and runs the epilogue.  The half goes over in EXCH_ROUNDS rounds of
+        // RECV_COLS columns (one round up to BN = 128).  Receive buffer: 128 rows x RECV_COLS
+        // floats, 16-byte chunk c of row r stored at c ^ (r & 7), so the 32 rows a warp touches
+        // at once spread over all banks.
+        constexpr int HB = C::RECV_COLS;  // floats per receive-buffer row
+        constexpr int GR = HB / 32;       // 32-column groups per round
+        constexpr int GH = BN / 64;       // 32-column groups per half
         const int acc = h & 1;
         if (!lcd::mbar_wait(&tfull[acc], (h >> 1) & 1, p.err)) {
           ok = false;
@@ -1066,20 +1074,23 @@ __device__ __forceinline__ void gemm_body(const Src& src) {
         const int row = q * 32 + lane;
         const uint32_t sw = (uint32_t)(row & 7);
         const uint32_t peer = rank ^ 1u;
-        // (1) the peer's half, once the peer has consumed what this CTA sent for the last tile
-        if (!lcd::mbar_wait_cluster(recv_free, (h & 1) ^ 1, p.err)) {
+#pragma unroll 1
+        for (int rd = 0; ok && rd < C::EXCH_ROUNDS; rd++, xr++) {
+        // (1) this round's columns of the peer's half, once the peer has consumed what this CTA
+        // sent it last round
+        if (!lcd::mbar_wait_cluster(recv_free, (xr & 1) ^ 1, p.err)) {
           ok = false;
           break;
         }
         {
           const uint32_t dst = lcd::mapa_shared(lcd::smem_u32(recv + row * HB), peer);
-          uint32_t r[GH][32];
+          uint32_t r[GR][32];
 #pragma unroll
-          for (int gl = 0; gl < GH; gl++)
-            lcd::tmem_ld_32x32b_x32(lane_base + acc * BN + (peer * GH + gl) * 32, r[gl]);
+          for (int gl = 0; gl < GR; gl++)
+            lcd::tmem_ld_32x32b_x32(lane_base + acc * BN + (peer * GH + rd * GR + gl) * 32, r[gl]);
           lcd::tmem_ld_wait();
 #pragma unroll
-          for (int gl = 0; gl < GH; gl++) {
+          for (int gl = 0; gl < GR; gl++) {
 #pragma unroll
             for (int k = 0; k < 8; k++) {
               const uint32_t chunk = (uint32_t)(gl * 8) + ((uint32_t)k ^ sw);
@@ -1089,15 +1100,16 @@ __device__ __forceinline__ void gemm_body(const Src& src) {
           }
         }
         lcd::mbar_arrive_remote(lcd::mapa_shared(lcd::smem_u32(recv_full), peer));
-        // (2) this CTA's half: its own accumulator plus the peer's, then the epilogue
-        if (!lcd::mbar_wait_cluster(recv_full, h & 1, p.err)) {
+        // (2) the same columns of this CTA's half: its own accumulator plus the peer's, then the
+        // epilogue
+        if (!lcd::mbar_wait_cluster(recv_full, xr & 1, p.err)) {
           ok = false;
           break;
         }
         const float* src = recv + row * HB;
 #pragma unroll 1
-        for (int gl = 0; gl < GH; gl++) {
-          const int g = (int)rank * GH + gl;
+        for (int gl = 0; gl < GR; gl++) {
+          const int g = (int)rank * GH + rd * GR + gl;
           uint32_t r[32];
           lcd::tmem_ld_32x32b_x32(lane_base + acc * BN + g * 32, r);
           lcd::tmem_ld_wait();
@@ -1132,6 +1144,8 @@ __device__ __forceinline__ void gemm_body(const Src& src) {
           }
         }
         lcd::mbar_arrive_remote(lcd::mapa_shared(lcd::smem_u32(recv_free), peer));
+        }
+        if (!ok) break;
         lcd::tc_fence_before();
         __syncwarp();
         if (lane == 0) lcd::mbar_arrive(&tempty[acc]);
@@ -1598,7 +1612,7 @@ lc_status launch_kernel(lc_context* ctx, cudaStream_t s, const CUtensorMap& ta, 
   cudaLaunchAttribute at[2];
   cudaLaunchConfig_t cfg = launch_config<BN, TF32X3, EPI, PAIR>(s, grid, at);
   cudaError_t e = cudaLaunchKernelEx(&cfg, gemm_tc_kernel<BN, TF32X3, EPI, PAIR>, ta, tb, p);
-  lc::record_launch(ctx, PAIR ? (BN == 64 ? "gemm_bf16_pair_n64" : "gemm_bf16_pair_n128")
+  lc::record_launch(ctx, PAIR ? (BN == 64 ? "gemm_bf16_pair_n64" : BN == 128 ? "gemm_bf16_pair_n128" : "gemm_bf16_pair_n256")
                          : TF32X3 ? (BN == 64 ? "gemm_tf32x3_n64" : "gemm_tf32x3_n128")
                                   : (BN == 64 ? "gemm_bf16_n64" : BN == 128 ? "gemm_bf16_n128" : "gemm_bf16_n256"));
   if (e != cudaSuccess) return lc::cuda_fail(e, "gemm launch");
@@ -1794,9 +1808,10 @@ lc_status plan_gemm(lc_context* ctx, const lc::GemmProblem& pr, lc_contract_plan
     return e != nullptr && e[0] == '0';
   }();
   int64_t pair_clusters = 0;
-  if (!dry_run && !tf32x3 && splits == 2 && bn <= 128 && pr.epi != 2 && !env_no_pair) {
-    const int cap = bn == 64 ? (pr.epi == 0 ? pair_capacity<64, 0>(ctx) : pair_capacity<64, 1>(ctx))
-                             : (pr.epi == 0 ? pair_capacity<128, 0>(ctx) : pair_capacity<128, 1>(ctx));
+  if (!dry_run && !tf32x3 && splits == 2 && pr.epi != 2 && !env_no_pair) {
+    const int cap = bn == 64    ? (pr.epi == 0 ? pair_capacity<64, 0>(ctx) : pair_capacity<64, 1>(ctx))
+                    : bn == 128 ? (pr.epi == 0 ? pair_capacity<128, 0>(ctx) : pair_capacity<128, 1>(ctx))
+                                : (pr.epi == 0 ? pair_capacity<256, 0>(ctx) : pair_capacity<256, 1>(ctx));
     pair_clusters = std::min<int64_t>({tiles, (int64_t)cap, (ctx->sm_count - pr.reserve_sms) / 2});
   }
   const bool pair = pair_clusters > 0;
@@ -2020,10 +2035,12 @@ lc_status gemm_run(lc_context* ctx, cudaStream_t s, const GemmProblem& pr, lc_co
          : pr.epi == 1 ? launch_2sm<1>(ctx, s, ta, tb, p, grid)
                        : launch_2sm<2>(ctx, s, ta, tb, p, grid);
   } else if (pair) {
-    st = bn == 64 ? (pr.epi == 0 ? launch_kernel<64, false, 0, true>(ctx, s, ta, tb, p, grid)
-                                 : launch_kernel<64, false, 1, true>(ctx, s, ta, tb, p, grid))
-                  : (pr.epi == 0 ? launch_kernel<128, false, 0, true>(ctx, s, ta, tb, p, grid)
-                                 : launch_kernel<128, false, 1, true>(ctx, s, ta, tb, p, grid));
+    st = bn == 64    ? (pr.epi == 0 ? launch_kernel<64, false, 0, true>(ctx, s, ta, tb, p, grid)
+                                    : launch_kernel<64, false, 1, true>(ctx, s, ta, tb, p, grid))
+         : bn == 128 ? (pr.epi == 0 ? launch_kernel<128, false, 0, true>(ctx, s, ta, tb, p, grid)
+                                    : launch_kernel<128, false, 1, true>(ctx, s, ta, tb, p, grid))
+                     : (pr.epi == 0 ? launch_kernel<256, false, 0, true>(ctx, s, ta, tb, p, grid)
+                                    : launch_kernel<256, false, 1, true>(ctx, s, ta, tb, p, grid));
   } else if (tf32x3) {
     st = bn == 64 ? launch_kernel<64, true, 0, false>(ctx, s, ta, tb, p, grid)
                   : launch_kernel<128, true, 0, false>(ctx, s, ta, tb, p, grid);

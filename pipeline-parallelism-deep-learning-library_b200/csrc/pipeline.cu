@@ -487,12 +487,12 @@ lc_status decide_fuse(lc_pipeline* p) {
         st = gemm_plan_shape(p->ctx, dgrad_problem(p, l, 0, mb, p->dP[l - 1]), &d.bn, &d.splits, &d.swap);
         if (st) return st;
       }
-      // A wider tile covers the group's rows (up to 128), so each weight tile is read by one CTA
-      // (pair) for two microbatches; with 64-wide tiles each CTA also re-reads its slice of the
+      // A wider tile covers the group's rows (up to 256), so each weight tile is read by one CTA
+      // pair for the whole group; with 64-wide tiles each CTA also re-reads its slice of the
       // activations, which made the per-SM load, not the DRAM, the limit.
       if (!env_narrow)
         for (lc_pipeline::Shape* sh : {&p->fwd_shape[l], &p->dgrad_shape[l]})
-          if (sh->bn == 64 && sh->swap > 0) sh->bn = (int32_t)std::min<uint64_t>(128, 64 * want);
+          if (sh->bn == 64 && sh->swap > 0) sh->bn = (int32_t)std::min<uint64_t>(256, 64 * want);
     }
   }
   p->fuse = want;

@@ -71,6 +71,14 @@ class lc_contract_plan(C.Structure):
                 ("b_major", C.c_int32)]
 
 
+class lc_epilogue(C.Structure):
+    _fields_ = [("kind", C.c_int32), ("aux", C.c_void_p), ("aux2", C.c_void_p), ("lr", C.c_float),
+                ("tile_n", C.c_int32), ("splits", C.c_int32), ("swap", C.c_int32)]
+
+
+EPI_NONE, EPI_RELU, EPI_RELU_MASK, EPI_SGD = 0, 1, 2, 3
+
+
 class lc_pipeline_config(C.Structure):
     _fields_ = [("layers", C.c_uint64), ("width", C.c_uint64), ("widths", C.POINTER(C.c_uint64)),
                 ("microbatch", C.c_uint64),
@@ -105,6 +113,7 @@ def _sig(L):
         "lc_encode_gemm": (s, [_vp, _vp, f, _V, _V, f, _V]),
         "lc_gemm": (s, [_vp, f, _V, _V, f, _V]),
         "lc_encode_gemm_noalloc": (s, [_vp, _vp, f, _V, _V, f, _V]),
+        "lc_encode_gemm_fused": (s, [_vp, _vp, f, _V, _V, f, _V, C.POINTER(lc_epilogue)]),
         "lc_encode_materialize": (s, [_vp, _vp, _V, _V]),
         "lc_materialize": (s, [_vp, _V, _V]),
         "lc_encode_conjugate": (s, [_vp, _vp, _V, _V]),
@@ -357,6 +366,20 @@ def encode_gemm_noalloc(ctx: Context, stream, alpha, a, b, beta, c):
     Calls that may run concurrently race on those arrays; the first call on a device does set-up."""
     a, b, c = as_view(a), as_view(b), as_view(c)
     check(load().lc_encode_gemm_noalloc(ctx.h, _stream(stream), float(alpha), a.ref(), b.ref(), float(beta), c.ref()))
+
+
+def encode_gemm_fused(ctx: Context, stream, alpha, a, b, beta, c, kind: int, aux=None, aux2=None, lr=0.0,
+                      tile_n=0, splits=0, swap=0):
+    """encode_gemm with a fused epilogue (EPI_RELU, EPI_RELU_MASK with `aux` the bf16 mask source,
+    EPI_SGD with C the f32 master weights and `aux2` their bf16 copy); tile_n / splits / swap pin
+    the plan (0 = the planner's choice)."""
+    a, b, c = as_view(a), as_view(b), as_view(c)
+    xv = as_view(aux) if aux is not None else None
+    yv = as_view(aux2) if aux2 is not None else None
+    e = lc_epilogue(int(kind), C.addressof(xv.c) if xv is not None else None,
+                    C.addressof(yv.c) if yv is not None else None, float(lr), int(tile_n), int(splits), int(swap))
+    check(load().lc_encode_gemm_fused(ctx.h, _stream(stream), float(alpha), a.ref(), b.ref(), float(beta), c.ref(),
+                                      C.byref(e)))
 
 
 def gemm(ctx: Context, alpha, a, b, beta, c):

@@ -179,6 +179,35 @@ def test_argmax_goldens(case):
     assert O.argmax(x) == case["expected"]
 
 
+def complex_case(case) -> np.ndarray:
+    """The n complex values of a transcribed argmax_complex case (interleaved f32 pairs)."""
+    z = np.empty((case["n"], 2), np.float32)
+    z[:, 0] = f32(case["fill"][0])
+    z[:, 1] = f32(case["fill"][1])
+    for i, re, im in case["set"]:
+        z[i] = (f32(re), f32(im))
+    return z
+
+
+@pytest.mark.parametrize("case", G["argmax_complex"]["cases"])
+def test_argmax_complex_goldens(case):
+    z = complex_case(case)
+    for kind, want in case["expected"].items():
+        assert O.argmax_complex(z, O.MAG_L1 if kind == "l1" else O.MAG_HYPOT) == want, (case["cite"], kind)
+
+
+def test_mag32_formulas():
+    # tests/argmax_test.rs:51-72: NaN parts give NaN, hi == 0 gives 0, an infinite part gives inf,
+    # and the scaled hypot stays finite where re^2 + im^2 would overflow
+    assert np.isnan(O.mag32(np.nan, 1.0, O.MAG_HYPOT)) and np.isnan(O.mag32(1.0, np.nan, O.MAG_L1))
+    assert O.mag32(-0.0, 0.0, O.MAG_HYPOT) == 0.0
+    assert O.mag32(np.inf, np.nan, O.MAG_L1) != O.mag32(np.inf, np.nan, O.MAG_L1)
+    assert O.mag32(np.inf, 3.0, O.MAG_HYPOT) == np.inf
+    assert O.mag32(3.0, -4.0, O.MAG_HYPOT) == 5.0 and O.mag32(3.0, -4.0, O.MAG_L1) == 7.0
+    big = float(np.float32(2e38))  # hypot 2.83e38: finite, while big * big overflows
+    assert np.isfinite(O.mag32(big, big, O.MAG_HYPOT))
+
+
 def test_argmax_nan_and_ties():
     # tests/argmax_test.rs:316-362 style cases
     x = np.ones(10, np.float32)
