@@ -228,6 +228,20 @@ def op_figures(hbm_peak, tc_peak):
     tf = 2 * n ** 3 / (ms * 1e-3) / 1e12
     out["gemm_bf16_8192"] = {"ms": ms, "tflops": tf, "frac_of_measured_bf16": tf / tc_peak}
     del a, b, c
+    # The f32 path's denominator: the tensor cores' tf32 rate, measured here as cuBLAS's tf32
+    # 8192^3 product (the same kind of figure as the measured bf16 peak).  3xTF32 issues three
+    # tf32 products per f32 product, so an f32 figure's roofline is a third of it.
+    prev = torch.backends.cuda.matmul.allow_tf32
+    torch.backends.cuda.matmul.allow_tf32 = True
+    a = torch.randn(n, n, device="cuda")
+    b = torch.randn(n, n, device="cuda")
+    c = torch.empty(n, n, device="cuda")
+    ms = time_launches(lambda: torch.matmul(a, b, out=c), torch.cuda.current_stream(), 10)
+    torch.backends.cuda.matmul.allow_tf32 = prev
+    tf32_peak = 2 * n ** 3 / (ms * 1e-3) / 1e12
+    out["tf32_peak_cublas_8192"] = {"ms": ms, "tflops": tf32_peak,
+                                    "what": "cuBLAS tf32 8192^3, the denominator of the f32 (3xTF32) figures"}
+    del a, b, c
     # f32 1024^3 (3xTF32) and the permuting contraction
     a = torch.rand(1024, 1024, device="cuda") * 2 - 1
     b = torch.rand(1024, 1024, device="cuda") * 2 - 1
@@ -275,6 +289,8 @@ def op_figures(hbm_peak, tc_peak):
     for k, v in out.items():
         if "gbs" in v:
             v["frac_of_measured_hbm"] = v["gbs"] / hbm_peak
+        if k.startswith("contract_f32"):
+            v["frac_of_tf32x3_roofline"] = 3 * v["tflops"] / tf32_peak
     del x, xp, dst, dst2, am, y
     ctx.close()
     torch.cuda.empty_cache()
@@ -501,6 +517,18 @@ def main():
     launches = p.debug_launches() - launches0
     ms_e2e, losses_e2e = timed(args.steps, False)
     clocks = clk.summary()
+    # one more step, untimed, with every op's compute bracketed by CUDA events: where each stage
+    # spends the step (its busy time against the 1F1B fill/drain and transfer waits)
+    p.set_trace(True)
+    p.step(x_dev, t_dev, on_device=True)
+    from linalg_b200.pipeline import trace_summary
+    stage_trace = trace_summary(p.trace(), p.last_step_ms)
+    p.set_trace(False)
+    if world > 1:
+        gathered = [None] * world
+        dist.all_gather_object(gathered, stage_trace)
+    else:
+        gathered = [stage_trace]
     value = args.steps * BATCH / (ms * 1e-3)
     e2e = args.steps * BATCH / (ms_e2e * 1e-3)
     if world > 1:
@@ -539,6 +567,7 @@ def main():
         }
         if world == 1:
             line["roofline_one_microbatch"] = roof_one
+        line["stage_trace"] = gathered
         if cpu_v is not None:
             line["cpu_baseline"] = {"value": cpu_v, "unit": "samples/s", "cores": 1, "kind": "port",
                                     "sample": f"one microbatch x one layer bf16 product ({cpu_s:.2f} s, 1 thread), "

@@ -148,6 +148,11 @@ typedef enum lc_epilogue_kind {
     LC_EPI_SGD = 3,        /* C (f32 master weights) = C - lr*(alpha*A*B); aux2 (bf16) = bf16(C)
                               (16-bit inputs; beta unused): the weight gradient with `sgd_step`
                               and `convert` fused (crates/cpu/src/lib.rs:474-533) */
+    LC_EPI_GELU = 4,       /* pre = alpha*A*B + beta*C; aux2 (optional) = pre; C = gelu(pre) (f32):
+                              a layer's forward, `gemm` then `gelu` (crates/pipeline/src/lib.rs:
+                              176-178; crates/cpu/src/lib.rs:809-853) */
+    LC_EPI_GELU_BACKWARD = 5 /* C = gelu_backward(pre = aux, dy = alpha*A*B) (f32, beta 0): the data
+                              gradient of layer l+1 fused with layer l's `gelu_backward` (:211, 220) */
 } lc_epilogue_kind;
 typedef struct lc_epilogue {
     int32_t kind;          /* lc_epilogue_kind */
@@ -172,8 +177,10 @@ lc_status lc_encode_gemm_fused(lc_context* ctx, void* stream, float alpha, const
  * or whose operands would need staging copies (no unit stride, or starts/strides not 16-byte
  * aligned), fails with LC_ERR_INVALID_ARGUMENT and launches nothing.  The arrays are shared by
  * every context, stream and thread of the process: calls whose kernels may overlap race and
- * give wrong results, so serialise them.  The first call on a device does set-up (it looks up
- * the arrays' device addresses); make it before any stream capture. */
+ * give wrong results, so serialise them.  The first call on a device does set-up: it looks up
+ * the arrays' device addresses, and under CUDA's default lazy module loading that lookup is what
+ * loads the arrays onto the device (16 MiB + 32 KiB, held until the process exits).  Make that
+ * first call before reserving the card's memory and before any stream capture. */
 lc_status lc_encode_gemm_noalloc(lc_context* ctx, void* stream, float alpha, const lc_view* a,
                                  const lc_view* b, float beta, const lc_view* c);
 
@@ -318,6 +325,14 @@ lc_status lc_pipeline_step(lc_pipeline* p, const float* x, const float* target_o
 lc_status lc_pipeline_get_output(lc_pipeline* p, float* host_y);
 /* Device time of the last step in milliseconds (CUDA events on the stage's compute stream). */
 lc_status lc_pipeline_last_step_ms(lc_pipeline* p, float* ms);
+/* Step trace (no reference counterpart; the reference's pipeline has no timing): with `on`,
+ * every later step records CUDA events around each op's compute and each layer's weight update
+ * (a few microseconds of event records per op).  lc_pipeline_trace then gives the last step's
+ * records, 4 floats each: kind (1 forward, -1 backward, 2 weight update), first microbatch of
+ * the op's group (or the global layer index of an update), start and end in ms from the step's
+ * start.  `out` NULL: only *n is set; otherwise `cap` (records) must hold *n of them. */
+lc_status lc_pipeline_set_trace(lc_pipeline* p, int32_t on);
+lc_status lc_pipeline_trace(lc_pipeline* p, float* out, uint64_t cap, uint64_t* n);
 /* The stage's compute stream (cudaStream_t); every step starts and ends on it. */
 void* lc_pipeline_stream(lc_pipeline* p);
 /* Kernel launches the stage has issued since creation (its `debug_launches().len()`). */

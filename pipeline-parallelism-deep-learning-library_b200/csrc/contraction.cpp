@@ -592,13 +592,17 @@ lc_status gemm_fused_impl(lc_context* ctx, void* stream, float alpha, const lc_v
   }
   lc_status st = prepare(a, b, &c16);
   if (st) return st;
-  if (e->kind < LC_EPI_NONE || e->kind > LC_EPI_SGD) return fail(LC_ERR_INVALID_ARGUMENT, "unknown epilogue kind");
+  if (e->kind < LC_EPI_NONE || e->kind > LC_EPI_GELU_BACKWARD) return fail(LC_ERR_INVALID_ARGUMENT, "unknown epilogue kind");
   if (e->tile_n != 0 && e->tile_n != 64 && e->tile_n != 128 && e->tile_n != 256)
     return fail(LC_ERR_INVALID_ARGUMENT, "tile_n is 0, 64, 128 or 256");
   if (e->splits < 0) return fail(LC_ERR_INVALID_ARGUMENT, "negative split count");
   const bool sixteen = a->dtype != LC_F32;
   if ((e->kind == LC_EPI_RELU_MASK || e->kind == LC_EPI_SGD) && !sixteen)
     return fail(LC_ERR_DTYPE, "the mask and SGD epilogues take bf16 or f16 inputs");
+  if ((e->kind == LC_EPI_GELU || e->kind == LC_EPI_GELU_BACKWARD) && sixteen)
+    return fail(LC_ERR_DTYPE, "the GELU epilogues take f32 operands");
+  if (e->kind == LC_EPI_GELU_BACKWARD && beta != 0.0f)
+    return fail(LC_ERR_INVALID_ARGUMENT, "the GELU backward epilogue takes beta = 0");
   Groups g;
   if ((st = groups_from_gemm(*a, *b, c16, &g))) return st;
   Plan plan;
@@ -629,6 +633,19 @@ lc_status gemm_fused_impl(lc_context* ctx, void* stream, float alpha, const lc_v
       pr.aux2 = e->aux2->data;
       pr.lr = e->lr;
       pr.c_dtype = LC_F32;
+      break;
+    case LC_EPI_GELU:
+      if (e->aux2 != nullptr) {
+        if ((st = same_layout_as_c(e->aux2, *c, LC_F32, "aux2 (the pre-activation output)"))) return st;
+        if (e->aux2->data == c->data) return fail(LC_ERR_ALIAS, "aux2 shares C's storage");
+        pr.aux2 = e->aux2->data;
+      }
+      pr.epi = 3;
+      break;
+    case LC_EPI_GELU_BACKWARD:
+      if ((st = same_layout_as_c(e->aux, *c, LC_F32, "aux (the pre-activation)"))) return st;
+      pr.epi = 4;
+      pr.aux = e->aux->data;
       break;
     default:
       break;

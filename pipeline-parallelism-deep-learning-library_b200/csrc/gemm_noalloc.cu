@@ -38,7 +38,9 @@ struct DeviceScratch {
 std::mutex g_mu;
 DeviceScratch g_scratch[kMaxDevices];
 
-// Device addresses of the arrays on `device`, looked up once per device.
+// Device addresses of the arrays on `device`, looked up once per device.  With lazy module
+// loading (CUDA's default) the first lookup also loads this file's module on the device, which
+// is when the arrays' memory is reserved there.
 lc_status scratch_of(int device, DeviceScratch* out) {
   if (device < 0 || device >= kMaxDevices) return lc::fail(LC_ERR_INVALID_ARGUMENT, "device ordinal out of range");
   std::lock_guard<std::mutex> g(g_mu);

@@ -31,6 +31,7 @@
 #include <type_traits>
 #include <unordered_map>
 
+#include "activation.cuh"
 #include "gemm.h"
 #include "internal.h"
 #include "ptx.cuh"
@@ -183,12 +184,17 @@ __device__ __forceinline__ float finish(const KParams& p, float acc, float cold)
 //   1  C = alpha * acc where aux > 0, else +0 (aux: bf16 laid out like C) -- the ReLU derivative
 //      fused into the data-gradient product;
 //   2  master = master - lr * (alpha * acc), aux2 = bf16(master) (aux: f32 master, aux2: bf16 copy,
-//      both laid out like C; C itself is unused) -- the SGD step fused into the weight gradient.
-// `old` is what the variant reads before it writes: C (EPI 0, beta != 0), the mask (1), master (2).
+//      both laid out like C; C itself is unused) -- the SGD step fused into the weight gradient;
+//   3  pre = alpha * acc + beta * C, aux2 = pre (when set), C = gelu(pre) -- a GELU layer's forward
+//      (f32: C and aux2 f32);
+//   4  C = (alpha * acc) * gelu'(aux) (aux: f32 pre-activation laid out like C) -- the data
+//      gradient through a GELU layer's derivative (f32).
+// `old` is what the variant reads before it writes: C (EPI 0 and 3, beta != 0), the mask (1),
+// master (2), the pre-activation (4).
 
 template <int EPI>
 __device__ __forceinline__ float read_old(const KParams& p, int64_t idx) {
-  if constexpr (EPI == 0) return p.beta != 0.0f ? load_c(p, idx) : 0.0f;
+  if constexpr (EPI == 0 || EPI == 3) return p.beta != 0.0f ? load_c(p, idx) : 0.0f;
   else if constexpr (EPI == 1) return __uint_as_float(((uint32_t) static_cast<const uint16_t*>(p.aux)[idx]) << 16);
   else return static_cast<const float*>(p.aux)[idx];
 }
@@ -199,6 +205,12 @@ __device__ __forceinline__ void write_new(const KParams& p, int64_t idx, float a
     store_c(p, idx, finish(p, acc, old));
   } else if constexpr (EPI == 1) {
     store_c(p, idx, old > 0.0f ? __fmul_rn(p.alpha, acc) : 0.0f);
+  } else if constexpr (EPI == 3) {
+    const float pre = finish(p, acc, old);
+    if (p.aux2 != nullptr) static_cast<float*>(p.aux2)[idx] = pre;
+    store_c(p, idx, lcd::gelu1(pre));
+  } else if constexpr (EPI == 4) {
+    store_c(p, idx, __fmul_rn(__fmul_rn(p.alpha, acc), lcd::gelu_prime1(old)));
   } else {
     const float w = __fsub_rn(old, __fmul_rn(p.lr, __fmul_rn(p.alpha, acc)));
     static_cast<float*>(const_cast<void*>(p.aux))[idx] = w;
@@ -216,7 +228,7 @@ __device__ __forceinline__ void write_new(const KParams& p, int64_t idx, float a
 //    kernel rows, touch 32 consecutive elements per store.
 template <int EPI>
 __device__ __forceinline__ void store_row(const KParams& p, const float (&v)[32], int64_t base, int32_t cnt) {
-  if (p.vec && cnt == 32) {
+  if (EPI < 3 && p.vec && cnt == 32) {
     if constexpr (EPI == 2) {
       float* master = static_cast<float*>(const_cast<void*>(p.aux)) + base;
       uint16_t* wb = static_cast<uint16_t*>(p.aux2) + base;
@@ -428,6 +440,21 @@ __device__ __forceinline__ void store_tile32(const KParams& p, const float (&v)[
     for (int i = 0; i < 8; i++)
       if (4 * i + rr < rows)
         *reinterpret_cast<float4*>(raw + (int64_t)(4 * i + rr) * raw_ld + cc) = make_float4(x[i][0], x[i][1], x[i][2], x[i][3]);
+    return;
+  } else if constexpr (EPI >= 3) {
+    // the GELU variants, element by element from the transposed block (lane: 4 consecutive
+    // columns of rows 4i + lane / 8)
+#pragma unroll
+    for (int i = 0; i < 8; i++) {
+      if (4 * i + rr >= rows) continue;
+      const int64_t idx = base + (int64_t)(4 * i + rr) * p.c_ms + cc;
+      float o[4];
+      const bool reads = EPI == 4 || p.beta != 0.0f;
+#pragma unroll
+      for (int e = 0; e < 4; e++) o[e] = reads ? read_old<EPI>(p, idx + e) : 0.0f;
+#pragma unroll
+      for (int e = 0; e < 4; e++) write_new<EPI>(p, idx + e, x[i][e], o[e]);
+    }
     return;
   } else {
     // the values the epilogue reads (C for beta, the mask, the master weights), all in flight together
@@ -1167,14 +1194,14 @@ __device__ __forceinline__ void gemm_body(const Src& src) {
         lcd::tc_fence_after();
         // The epilogue's reads (master weights, mask, old C) wait on HBM group after group; pull
         // the next unit's rows into L2 now, a tile ahead, so that they come from L2 then.
-        if (!split_mode && p.vec && (EPI != 0 || p.beta != 0.0f) && u + u_step < p.units) {
+        if (!split_mode && p.vec && ((EPI != 0 && EPI != 3) || p.beta != 0.0f) && u + u_step < p.units) {
           int32_t b2, s2, tm2, tn2;
           unit_coords(p, u + u_step, &b2, &s2, &tm2, &tn2);
           const int32_t m2 = tile_row0(tm2) + q * 32 + lane;
           const int32_t n2 = tn2 * BN;
           if (m2 < p.M && n2 < p.N) {
-            const int es = (EPI == 2 || p.c_dtype == LC_F32) ? 4 : 2;
-            const char* src = static_cast<const char*>(EPI == 0 ? static_cast<const void*>(p.c) : p.aux) +
+            const int es = (EPI == 2 || EPI == 4 || p.c_dtype == LC_F32) ? 4 : 2;
+            const char* src = static_cast<const char*>((EPI == 0 || EPI == 3) ? static_cast<const void*>(p.c) : p.aux) +
                               (p.c_off + (int64_t)b2 * p.c_bs + (int64_t)m2 * p.c_ms + n2) * es;
             const int32_t bytes = min(BN, p.N - n2) * es;
             for (int32_t off = 0; off < bytes; off += 128) asm volatile("prefetch.global.L2 [%0];" ::"l"(src + off));
@@ -1919,14 +1946,20 @@ lc_status plan_gemm(lc_context* ctx, const lc::GemmProblem& pr, lc_contract_plan
     p.fb_bs = B.batch > 1 ? B.batch_stride : 0;
     p.K = (int64_t)pr.k;
   }
-  if (tf32x3 && pr.epi != 0) return fail(LC_ERR_INVALID_ARGUMENT, "fused epilogues take 16-bit inputs");
-  if (pr.epi < 0 || pr.epi > 2) return fail(LC_ERR_INVALID_ARGUMENT, "unknown epilogue");
+  if (tf32x3 && (pr.epi == 1 || pr.epi == 2))
+    return fail(LC_ERR_INVALID_ARGUMENT, "the mask and SGD epilogues take 16-bit inputs");
+  if (!tf32x3 && pr.epi >= 3) return fail(LC_ERR_INVALID_ARGUMENT, "the GELU epilogues take f32 inputs");
+  if (pr.epi < 0 || pr.epi > 4) return fail(LC_ERR_INVALID_ARGUMENT, "unknown epilogue");
   {
     // 16-byte vector epilogue: C's columns contiguous, every row start a multiple of 8 elements
     // from 16-byte-aligned bases (8 covers both 2- and 4-byte elements)
     auto al16 = [](const void* q) { return (reinterpret_cast<uintptr_t>(q) & 15u) == 0; };
     const bool strides8 = (p.c_off % 8) == 0 && (p.c_ms % 8) == 0 && (pr.batch == 1 || (p.c_bs % 8) == 0);
-    const bool ptrs = pr.epi == 0 ? al16(pr.c) : pr.epi == 1 ? al16(pr.c) && al16(pr.aux) : al16(pr.aux) && al16(pr.aux2);
+    const bool ptrs = pr.epi == 0   ? al16(pr.c)
+                      : pr.epi == 1 ? al16(pr.c) && al16(pr.aux)
+                      : pr.epi == 2 ? al16(pr.aux) && al16(pr.aux2)
+                      : pr.epi == 3 ? al16(pr.c) && (pr.aux2 == nullptr || al16(pr.aux2))
+                                    : al16(pr.c) && al16(pr.aux);
     p.vec = (c_ns == 1 && strides8 && ptrs) ? 1 : 0;
     const bool tstrides8 = (p.c_off % 8) == 0 && (p.c_ns % 8) == 0 && (pr.batch == 1 || (p.c_bs % 8) == 0);
     p.tvec = (c_ms == 1 && c_ns != 1 && tstrides8 && ptrs && pr.epi != 2) ? 1 : 0;
@@ -2042,8 +2075,14 @@ lc_status gemm_run(lc_context* ctx, cudaStream_t s, const GemmProblem& pr, lc_co
                      : (pr.epi == 0 ? launch_kernel<256, false, 0, true>(ctx, s, ta, tb, p, grid)
                                     : launch_kernel<256, false, 1, true>(ctx, s, ta, tb, p, grid));
   } else if (tf32x3) {
-    st = bn == 64 ? launch_kernel<64, true, 0, false>(ctx, s, ta, tb, p, grid)
-                  : launch_kernel<128, true, 0, false>(ctx, s, ta, tb, p, grid);
+    auto tf32_by_bn = [&](auto epi_tag) {
+      constexpr int E = decltype(epi_tag)::value;
+      return bn == 64 ? launch_kernel<64, true, E, false>(ctx, s, ta, tb, p, grid)
+                      : launch_kernel<128, true, E, false>(ctx, s, ta, tb, p, grid);
+    };
+    st = pr.epi == 0   ? tf32_by_bn(std::integral_constant<int, 0>{})
+         : pr.epi == 3 ? tf32_by_bn(std::integral_constant<int, 3>{})
+                       : tf32_by_bn(std::integral_constant<int, 4>{});
   } else {
     auto by_bn = [&](auto epi_tag) {
       constexpr int E = decltype(epi_tag)::value;
@@ -2072,7 +2111,9 @@ lc_status gemm_run(lc_context* ctx, cudaStream_t s, const GemmProblem& pr, lc_co
     cfg.numAttrs = 1;
     cudaError_t e = pr.epi == 0   ? cudaLaunchKernelEx(&cfg, splitk_reduce_kernel<0>, p)
                     : pr.epi == 1 ? cudaLaunchKernelEx(&cfg, splitk_reduce_kernel<1>, p)
-                                  : cudaLaunchKernelEx(&cfg, splitk_reduce_kernel<2>, p);
+                    : pr.epi == 2 ? cudaLaunchKernelEx(&cfg, splitk_reduce_kernel<2>, p)
+                    : pr.epi == 3 ? cudaLaunchKernelEx(&cfg, splitk_reduce_kernel<3>, p)
+                                  : cudaLaunchKernelEx(&cfg, splitk_reduce_kernel<4>, p);
     record_launch(ctx, "gemm_splitk_reduce");
     if (e == cudaSuccess) e = cudaGetLastError();
     if (e != cudaSuccess) st = cuda_fail(e, "split-K reduce launch");

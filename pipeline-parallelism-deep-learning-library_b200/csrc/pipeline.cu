@@ -257,6 +257,12 @@ struct lc_pipeline {
   std::vector<Shape> fwd_shape, dgrad_shape;
   float last_ms = 0.0f;
   bool aborted = false;
+  // Step trace (lc_pipeline_set_trace): timing events around every op's compute and around the
+  // weight updates; after the step, one record per op of (kind, first microbatch, start, end) in
+  // ms from the step start.  kind: 1 forward, -1 backward, 2 weight update of one layer.
+  bool trace = false;
+  std::vector<cudaEvent_t> ev_t0, ev_t1;
+  std::vector<float> trace_rec;
 
   uint64_t win(uint64_t l) const { return widths[first + l]; }       // local layer l input width
   uint64_t wout(uint64_t l) const { return widths[first + l + 1]; }  // local layer l output width
@@ -454,12 +460,13 @@ lc_status run_products(lc_pipeline* p, cudaStream_t s, const std::vector<GemmPro
   return LC_OK;
 }
 
-// Microbatches per product.  Only a stage holding every layer in training mode groups them: its
-// 1F1B order is F(0) B(0) F(1) B(1) ..., the forwards only read weights nobody writes before the
-// step's weight updates, and B(m) needs nothing but F(m), so F(m) F(m+1) as one product followed
-// by B(m) B(m+1) as one product leaves every result unchanged (likewise for groups of four).
-// With several stages each microbatch crosses the link on its own and is computed alone.
-// LC_PIPE_FUSE=1 turns it off.
+// Microbatches per product (training mode).  The forwards only read weights nobody writes before
+// the step's weight updates, and B(m) needs nothing but F(m) (and, on a later stage, the
+// gradient of m from the next stage), so consecutive microbatches run as one taller product per
+// layer without changing any result: each group product keeps the one-microbatch product's split
+// count and orientation, so every element sees the same operations in the same order.  The
+// schedule is then 1F1B over the groups (local_order over microbatches / fuse units), each group
+// crossing a stage boundary as one transfer of its rows.  LC_PIPE_FUSE=1 turns it off.
 lc_status decide_fuse(lc_pipeline* p) {
   static const int env_fuse = [] {
     const char* e = getenv("LC_PIPE_FUSE");  // microbatches per product on one stage (1, 2 or 4)
@@ -472,7 +479,7 @@ lc_status decide_fuse(lc_pipeline* p) {
   const uint64_t mbs = p->cfg.microbatches, mb = p->cfg.microbatch;
   uint64_t want = env_fuse == 1 || env_fuse == 2 || env_fuse == 4 ? (uint64_t)env_fuse : kFuseDefault;
   while (want > 1 && mbs % want != 0) want /= 2;
-  if (!p->train_mode || p->world != 1) want = 1;
+  if (!p->train_mode) want = 1;
   if (want > 1) {
     // Each group product keeps the one-microbatch product's split count and orientation, so
     // every element is computed by the same operations in the same order.
@@ -482,9 +489,10 @@ lc_status decide_fuse(lc_pipeline* p) {
       lc_pipeline::Shape& f = p->fwd_shape[l];
       lc_status st = gemm_plan_shape(p->ctx, fwd_problem(p, l, 0, mb), &f.bn, &f.splits, &f.swap);
       if (st) return st;
-      if (l > 0) {
+      if (l > 0 || !p->is_first()) {
         lc_pipeline::Shape& d = p->dgrad_shape[l];
-        st = gemm_plan_shape(p->ctx, dgrad_problem(p, l, 0, mb, p->dP[l - 1]), &d.bn, &d.splits, &d.swap);
+        st = gemm_plan_shape(p->ctx, dgrad_problem(p, l, 0, mb, l > 0 ? p->dP[l - 1] : p->gsend), &d.bn, &d.splits,
+                             &d.swap);
         if (st) return st;
       }
       // A wider tile covers the group's rows (up to 256), so each weight tile is read by one CTA
@@ -728,6 +736,8 @@ lc_status lc_pipeline_destroy(lc_pipeline* p) {
   for (auto e : {p->ev_start, p->ev_end, p->ev_fwd_join, p->ev_bwd_join, p->ev_inputs})
     if (e) cudaEventDestroy(e);
   for (auto e : p->ev_work_join) cudaEventDestroy(e);
+  for (auto* v : {&p->ev_t0, &p->ev_t1})
+    for (auto e : *v) cudaEventDestroy(e);
   for (auto q : p->s_work)
     if (q) cudaStreamDestroy(q);
   if (p->s_fwd) cudaStreamDestroy(p->s_fwd);
@@ -801,6 +811,31 @@ lc_status lc_pipeline_get_output(lc_pipeline* p, float* host_y) {
   return LC_OK;
 }
 
+lc_status lc_pipeline_set_trace(lc_pipeline* p, int32_t on) {
+  if (!p) return fail(LC_ERR_INVALID_ARGUMENT, "null pipeline");
+  cudaSetDevice(p->device);
+  if (on && p->ev_t0.empty()) {
+    const size_t n = 2 * p->cfg.microbatches + p->count;
+    p->ev_t0.resize(n);
+    p->ev_t1.resize(n);
+    for (auto* v : {&p->ev_t0, &p->ev_t1})
+      for (auto& e : *v) CU(cudaEventCreate(&e));
+  }
+  p->trace = on != 0;
+  p->trace_rec.clear();
+  return LC_OK;
+}
+
+lc_status lc_pipeline_trace(lc_pipeline* p, float* out, uint64_t cap, uint64_t* n) {
+  if (!p || !n) return fail(LC_ERR_INVALID_ARGUMENT, "null argument");
+  const uint64_t have = p->trace_rec.size() / 4;
+  *n = have;
+  if (out == nullptr) return LC_OK;
+  if (cap < have) return fail(LC_ERR_INVALID_ARGUMENT, "trace buffer holds fewer records than the step made");
+  memcpy(out, p->trace_rec.data(), p->trace_rec.size() * sizeof(float));
+  return LC_OK;
+}
+
 lc_status lc_pipeline_last_step_ms(lc_pipeline* p, float* ms) {
   if (!p || !ms) return fail(LC_ERR_INVALID_ARGUMENT, "null argument");
   *ms = p->last_ms;
@@ -826,16 +861,13 @@ lc_status lc_pipeline_step(lc_pipeline* p, const float* x, const float* target_o
   const uint64_t fuse = p->fuse;
   std::vector<int64_t> order(2 * mbs);
   uint64_t n_ops = 0;
-  lc_status st = LC_OK;
-  if (fuse > 1) {
-    // one stage: 1F1B is F(m) B(m) in microbatch order; each op here covers `fuse` microbatches
-    for (uint64_t g = 0; g < mbs / fuse; g++) {
-      order[n_ops++] = (int64_t)(g * fuse) + 1;
-      order[n_ops++] = -((int64_t)(g * fuse) + 1);
-    }
-  } else {
-    st = lc_local_order((uint64_t)p->world, (uint64_t)p->rank, mbs, order.data(), order.size(), &n_ops);
-    if (st) return st;
+  // 1F1B over groups of `fuse` microbatches: op +-(u + 1) of the group schedule covers
+  // microbatches u * fuse .. u * fuse + fuse - 1, stored here as +-(first microbatch + 1)
+  lc_status st = lc_local_order((uint64_t)p->world, (uint64_t)p->rank, mbs / fuse, order.data(), order.size(), &n_ops);
+  if (st) return st;
+  for (uint64_t i = 0; i < n_ops; i++) {
+    const int64_t u = (order[i] > 0 ? order[i] : -order[i]) - 1;
+    order[i] = (order[i] > 0 ? 1 : -1) * (u * (int64_t)fuse + 1);
   }
   cudaStream_t cs = p->comp();
   const ncclDataType_t nt = p->train_mode ? ncclBfloat16 : ncclFloat32;
@@ -865,27 +897,30 @@ lc_status lc_pipeline_step(lc_pipeline* p, const float* x, const float* target_o
           to_bf16_kernel<<<blocks_for(p->ctx, rows * w0), 256, 0, fs>>>(p->x_dev + row0 * w0, (uint16_t*)in, rows * w0);
           record_launch(p->ctx, "pipeline_input_to_bf16");
         } else {
-          CU(cudaMemcpyAsync(in, p->x_dev + row0 * w0, mb * w0 * 4, cudaMemcpyDeviceToDevice, fs));
+          CU(cudaMemcpyAsync(in, p->x_dev + row0 * w0, rows * w0 * 4, cudaMemcpyDeviceToDevice, fs));
         }
       } else {
-        NC(nccl().Recv(in, mb * w0, nt, p->rank - 1, p->comm_fwd, p->s_fwd));
+        NC(nccl().Recv(in, rows * w0, nt, p->rank - 1, p->comm_fwd, p->s_fwd));
         CU(cudaEventRecord(p->ev_fr[m], p->s_fwd));
         CU(cudaStreamWaitEvent(fs, p->ev_fr[m], 0));
       }
+      const uint64_t ti = i;  // trace slot of this op
+      if (p->trace) CU(cudaEventRecord(p->ev_t0[ti], fs));
       if (p->train_mode) {
         std::vector<GemmProblem> probs;
         for (uint64_t l = 0; l < p->count; l++)
           probs.push_back(fuse > 1 ? shaped(fwd_problem(p, l, row0, rows), p->fwd_shape[l]) : fwd_problem(p, l, row0, mb));
         st = run_products(p, fs, probs);
       } else {
-        for (uint64_t l = 0; l < p->count && !st; l++) st = ref_forward(p, l, row0, mb);
+        for (uint64_t j = 0; j < fuse && !st; j++)
+          for (uint64_t l = 0; l < p->count && !st; l++) st = ref_forward(p, l, row0 + j * mb, mb);
       }
       if (st) break;
       void* outp = (uint8_t*)p->H[p->count] + row0 * wl * es;
       if (!p->is_last()) {
         CU(cudaEventRecord(p->ev_fd[m], fs));
         CU(cudaStreamWaitEvent(p->s_fwd, p->ev_fd[m], 0));
-        NC(nccl().Send(outp, mb * wl, nt, p->rank + 1, p->comm_fwd, p->s_fwd));
+        NC(nccl().Send(outp, rows * wl, nt, p->rank + 1, p->comm_fwd, p->s_fwd));
       } else if (p->train_mode) {
         // one launch per microbatch: its loss partials are summed exactly as without grouping
         for (uint64_t j = 0; j < fuse; j++) {
@@ -897,6 +932,7 @@ lc_status lc_pipeline_step(lc_pipeline* p, const float* x, const float* target_o
         }
       }
       CU(cudaEventRecord(p->ev_fdone[m], fs));
+      if (p->trace) CU(cudaEventRecord(p->ev_t1[ti], fs));
     } else {
       // backward of microbatch m on its own stream, after its forward (activations, masks, the
       // loss gradient) is complete
@@ -906,19 +942,20 @@ lc_status lc_pipeline_step(lc_pipeline* p, const float* x, const float* target_o
       const float* g_ref = nullptr;
       if (!p->is_last()) {
         void* gin = (uint8_t*)p->dP[p->train_mode ? p->count - 1 : 0] + row0 * wl * es;
-        NC(nccl().Recv(gin, mb * wl, nt, p->rank + 1, p->comm_bwd, p->s_bwd));
+        NC(nccl().Recv(gin, rows * wl, nt, p->rank + 1, p->comm_bwd, p->s_bwd));
         CU(cudaEventRecord(p->ev_br[m], p->s_bwd));
         CU(cudaStreamWaitEvent(bs, p->ev_br[m], 0));
         g_ref = (const float*)gin;
       } else {
         g_ref = p->t_dev + row0 * wl;  // reference mode: dy
       }
+      if (p->trace) CU(cudaEventRecord(p->ev_t0[i], bs));
       if (p->train_mode) {
         std::vector<GemmProblem> probs;
         for (uint64_t l = p->count; l-- > 0;) {
-          if (l > 0 && fuse > 1) probs.push_back(shaped(dgrad_problem(p, l, row0, rows, p->dP[l - 1]), p->dgrad_shape[l]));
-          else if (l > 0) probs.push_back(dgrad_problem(p, l, row0, mb, p->dP[l - 1]));
-          else if (!p->is_first()) probs.push_back(dgrad_problem(p, 0, row0, mb, p->gsend));
+          if (l == 0 && p->is_first()) continue;  // rank 0 discards layer 0's input gradient
+          GemmProblem g = dgrad_problem(p, l, row0, rows, l > 0 ? p->dP[l - 1] : p->gsend);
+          probs.push_back(fuse > 1 ? shaped(g, p->dgrad_shape[l]) : g);
         }
         st = run_products(p, bs, probs);
       } else {
@@ -935,10 +972,11 @@ lc_status lc_pipeline_step(lc_pipeline* p, const float* x, const float* target_o
         }
       }
       if (st) break;
+      if (p->trace) CU(cudaEventRecord(p->ev_t1[i], bs));
       if (!p->is_first()) {
         CU(cudaEventRecord(p->ev_bd[m], bs));
         CU(cudaStreamWaitEvent(p->s_bwd, p->ev_bd[m], 0));
-        NC(nccl().Send((uint8_t*)p->gsend + row0 * w0 * es, mb * w0, nt, p->rank - 1, p->comm_bwd, p->s_bwd));
+        NC(nccl().Send((uint8_t*)p->gsend + row0 * w0 * es, rows * w0, nt, p->rank - 1, p->comm_bwd, p->s_bwd));
       }
     }
   }
@@ -948,7 +986,11 @@ lc_status lc_pipeline_step(lc_pipeline* p, const float* x, const float* target_o
     CU(cudaStreamWaitEvent(cs, p->ev_work_join[i], 0));
   }
   if (!st && p->train_mode)
-    for (uint64_t l = 0; l < p->count && !st; l++) st = wgrad_layer(p, l);
+    for (uint64_t l = 0; l < p->count && !st; l++) {
+      if (p->trace) CU(cudaEventRecord(p->ev_t0[n_ops + l], cs));
+      st = wgrad_layer(p, l);
+      if (p->trace) CU(cudaEventRecord(p->ev_t1[n_ops + l], cs));
+    }
   if (!st && p->train_mode && p->is_last()) {
     loss_reduce_kernel<<<1, kMseThreads, 0, cs>>>(p->part, (int)(kMseBlocks * mbs), n_total, p->loss_dev);
     record_launch(p->ctx, "pipeline_loss_reduce");
@@ -963,6 +1005,20 @@ lc_status lc_pipeline_step(lc_pipeline* p, const float* x, const float* target_o
   lc_status wst = wait_step(p);
   if (st) return st;
   if (wst) return wst;
+  if (p->trace) {
+    p->trace_rec.clear();
+    const uint64_t n_w = p->train_mode ? p->count : 0;
+    for (uint64_t i = 0; i < n_ops + n_w; i++) {
+      float t0 = 0.0f, t1 = 0.0f;
+      CU(cudaEventElapsedTime(&t0, p->ev_start, p->ev_t0[i]));
+      CU(cudaEventElapsedTime(&t1, p->ev_start, p->ev_t1[i]));
+      const bool op = i < n_ops;
+      p->trace_rec.insert(p->trace_rec.end(),
+                          {op ? (order[i] > 0 ? 1.0f : -1.0f) : 2.0f,
+                           op ? (float)((order[i] > 0 ? order[i] : -order[i]) - 1) : (float)(p->first + i - n_ops), t0,
+                           t1});
+    }
+  }
   if (loss) *loss = (p->train_mode && p->is_last()) ? *p->loss_host : 0.0f;
   return LC_OK;
 }

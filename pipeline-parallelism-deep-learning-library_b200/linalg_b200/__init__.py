@@ -76,7 +76,7 @@ class lc_epilogue(C.Structure):
                 ("tile_n", C.c_int32), ("splits", C.c_int32), ("swap", C.c_int32)]
 
 
-EPI_NONE, EPI_RELU, EPI_RELU_MASK, EPI_SGD = 0, 1, 2, 3
+EPI_NONE, EPI_RELU, EPI_RELU_MASK, EPI_SGD, EPI_GELU, EPI_GELU_BACKWARD = 0, 1, 2, 3, 4, 5
 
 
 class lc_pipeline_config(C.Structure):
@@ -157,6 +157,8 @@ def _sig(L):
         "lc_pipeline_step": (s, [_vp, _vp, _vp, C.c_int32, C.POINTER(C.c_float)]),
         "lc_pipeline_get_output": (s, [_vp, _vp]),
         "lc_pipeline_last_step_ms": (s, [_vp, C.POINTER(C.c_float)]),
+        "lc_pipeline_set_trace": (s, [_vp, C.c_int32]),
+        "lc_pipeline_trace": (s, [_vp, _vp, C.c_uint64, C.POINTER(C.c_uint64)]),
         "lc_pipeline_init_weights": (s, [_vp, C.c_uint64, C.c_float]),
         "lc_pipeline_stream": (_vp, [_vp]),
         "lc_pipeline_debug_launches": (C.c_uint64, [_vp]),

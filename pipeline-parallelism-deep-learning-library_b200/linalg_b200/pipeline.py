@@ -121,3 +121,44 @@ class Pipeline:
         ms = C.c_float(0)
         check(load().lc_pipeline_last_step_ms(self.h, C.byref(ms)))
         return ms.value
+
+    def set_trace(self, on: bool = True):
+        """Record CUDA events around every op of later steps (see trace())."""
+        check(load().lc_pipeline_set_trace(self.h, 1 if on else 0))
+
+    def trace(self) -> np.ndarray:
+        """The last traced step: rows of (kind, first microbatch or layer, start ms, end ms), kind 1
+        forward, -1 backward, 2 weight update, times from the step's start on this stage."""
+        L = load()
+        n = C.c_uint64(0)
+        check(L.lc_pipeline_trace(self.h, None, 0, C.byref(n)))
+        out = np.zeros((n.value, 4), np.float32)
+        if n.value:
+            check(L.lc_pipeline_trace(self.h, out.ctypes.data_as(C.c_void_p), n.value, C.byref(n)))
+        return out
+
+
+def trace_summary(rec: np.ndarray, step_ms: float) -> dict:
+    """Busy time of a stage (the union of its ops' compute intervals, forwards, backwards and
+    weight updates) against its step time; the rest is time the stage had nothing it could run:
+    the 1F1B fill and drain, and waits on transfers."""
+    iv = sorted((float(a), float(b)) for _, _, a, b in rec)
+    busy, cur_a, cur_b = 0.0, None, None
+    for a, b in iv:
+        if cur_b is None or a > cur_b:
+            if cur_b is not None:
+                busy += cur_b - cur_a
+            cur_a, cur_b = a, b
+        else:
+            cur_b = max(cur_b, b)
+    if cur_b is not None:
+        busy += cur_b - cur_a
+    fwd = [b - a for k, _, a, b in rec if k == 1]
+    bwd = [b - a for k, _, a, b in rec if k == -1]
+    upd = [b - a for k, _, a, b in rec if k == 2]
+    first_bwd = min([a for k, _, a, b in rec if k == -1], default=0.0)
+    return {"step_ms": step_ms, "busy_ms": busy, "idle_ms": step_ms - busy,
+            "forward_ms_mean": float(np.mean(fwd)) if fwd else 0.0,
+            "backward_ms_mean": float(np.mean(bwd)) if bwd else 0.0,
+            "update_ms_total": float(np.sum(upd)) if upd else 0.0,
+            "first_backward_at_ms": first_bwd, "ops": int(len(rec))}
