@@ -274,6 +274,43 @@ lc_status lc_wire_write_header(lc_dtype dtype, const uint64_t* shape, uint32_t n
 lc_status lc_wire_parse_header(const uint8_t* bytes, uint64_t len, lc_dtype* dtype, uint64_t shape[8],
                                uint32_t* ndim, uint64_t* payload_offset);
 
+/* ---- host transports (crates/transport, the `Transport` trait crates/core/src/lib.rs:247-273) --
+ * Byte messages between pipeline ranks that are host threads or processes (the GPU pipeline's
+ * own data plane is NCCL).  Every failure is LC_ERR_TRANSPORT: a peer rank out of range or our
+ * own, a timeout, a peer that is gone, a bad handshake.  Messages from one source arrive in order
+ * and never merge with another source's.  A negative timeout waits forever. */
+typedef struct lc_transport lc_transport;
+/* `loopback(world)` (loopback.rs:21-28): `world` endpoints of one process in out[0..world). */
+lc_status lc_transport_loopback(uint32_t world, lc_transport** out);
+/* `localhost_mesh(world)` (tcp.rs:208-231): `world` endpoints connected over 127.0.0.1. */
+lc_status lc_transport_localhost_mesh(uint32_t world, lc_transport** out);
+/* `tcp_mesh_with_depth` (mesh.rs:38-87): this process's rank of a mesh whose rank r listens on
+ * addrs[r] ("a.b.c.d:port"); dials lower ranks, accepts higher ones, LNGM handshake, within
+ * `connect_timeout_ms`; `queue_depth` messages queue per peer before a send blocks (4 by default
+ * in the reference). */
+lc_status lc_transport_tcp_mesh(uint32_t rank, const char* const* addrs, uint32_t world,
+                                int64_t connect_timeout_ms, uint32_t queue_depth, lc_transport** out);
+/* Drops the endpoint: queued sends go out first, then the connections close. */
+lc_status lc_transport_destroy(lc_transport* t);
+uint32_t lc_transport_rank(const lc_transport* t);
+uint32_t lc_transport_world(const lc_transport* t);
+/* `send` / `send_parts` (core/src/lib.rs:252-262): one message, the concatenation of the parts;
+ * returns once copied (blocks while the peer's queue is full). */
+lc_status lc_transport_send(lc_transport* t, uint32_t dest, const void* bytes, uint64_t len);
+lc_status lc_transport_send_parts(lc_transport* t, uint32_t dest, const void* const* parts,
+                                  const uint64_t* lens, uint32_t n_parts);
+/* `recv_timeout` (:254): the oldest message from `src`, in a buffer the caller releases with
+ * lc_transport_free. */
+lc_status lc_transport_recv(lc_transport* t, uint32_t src, int64_t timeout_ms, uint8_t** data,
+                            uint64_t* len);
+void lc_transport_free(uint8_t* data);
+/* `send_tensor` / `recv_tensor` (crates/pipeline/src/lib.rs:71-98): a row-major device tensor
+ * downloaded, framed with the LNGL header and sent; received, its dtype and shape checked against
+ * `v` (LC_ERR_DTYPE / LC_ERR_SHAPE, LC_ERR_WIRE for a bad frame) and uploaded into it. */
+lc_status lc_transport_send_tensor(lc_transport* t, uint32_t dest, lc_context* ctx, const lc_view* v);
+lc_status lc_transport_recv_tensor(lc_transport* t, uint32_t src, int64_t timeout_ms, lc_context* ctx,
+                                   const lc_view* v);
+
 /* ---- 1F1B pipeline (crates/pipeline/src/lib.rs:100-230), one stage per GPU ---------------- */
 
 typedef struct lc_pipeline lc_pipeline;

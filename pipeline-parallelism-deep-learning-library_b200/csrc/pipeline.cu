@@ -547,51 +547,94 @@ lc_status wgrad_layer(lc_pipeline* p, uint64_t l) {
 
 // ---- reference-mode building blocks (the reference's Backend call sequence) -------------------
 
+// pre = x @ W, act = gelu(pre) (crates/pipeline/src/lib.rs:176-178).  GELU layers do both in one
+// product (the fused GELU epilogue stores pre and act, the same bits as gemm then gelu); ReLU
+// layers run the gemm and the standalone relu.
 lc_status ref_forward(lc_pipeline* p, uint64_t l, uint64_t row0, uint64_t rows) {
   const uint64_t k = p->win(l), n = p->wout(l);
   lc_view x = matrix_view((float*)p->H[l] + row0 * k, LC_F32, rows, k, rows * k * 4);
   lc_view w = matrix_view(p->master[l], LC_F32, k, n, k * n * 4);
   lc_view pre = matrix_view(p->pre[l] + row0 * n, LC_F32, rows, n, rows * n * 4);
   lc_view act = matrix_view((float*)p->H[l + 1] + row0 * n, LC_F32, rows, n, rows * n * 4);
+  if (p->cfg.activation == 0) {
+    lc_epilogue e{};
+    e.kind = LC_EPI_GELU;
+    e.aux2 = &pre;
+    return lc_encode_gemm_fused(p->ctx, p->comp(), 1.0f, &x, &w, 0.0f, &act, &e);
+  }
   lc_status st = lc_backend_gemm(p->ctx, p->comp(), &x, &w, &pre, 1.0f, 0.0f);
   if (st) return st;
-  return p->cfg.activation == 0 ? lc_gelu(p->ctx, p->comp(), &pre, &act) : lc_relu(p->ctx, p->comp(), &pre, &act);
+  return lc_relu(p->ctx, p->comp(), &pre, &act);
 }
 
-// g: incoming gradient (f32 [rows, n]); writes dx into `dx_out` (f32 [rows, k]) unless null.
-lc_status ref_backward(lc_pipeline* p, uint64_t l, uint64_t row0, uint64_t rows, const float* g, float* dx_out) {
-  const uint64_t k = p->win(l), n = p->wout(l);
-  lc_view pre = matrix_view(p->pre[l] + row0 * n, LC_F32, rows, n, rows * n * 4);
-  lc_view gv = matrix_view(const_cast<float*>(g), LC_F32, rows, n, rows * n * 4);
-  lc_view dpre = matrix_view(p->dbuf, LC_F32, rows, n, rows * n * 4);
-  lc_status st = p->cfg.activation == 0 ? lc_gelu_backward(p->ctx, p->comp(), &pre, &gv, &dpre)
-                                         : lc_relu_backward(p->ctx, p->comp(), &pre, &gv, &dpre);
-  if (st) return st;
-  // dW[k, n] += x^T [k, rows] @ dpre [rows, n]  (crates/pipeline/src/lib.rs:218, beta = 1)
-  lc_view xt{};
-  xt.data = (float*)p->H[l] + row0 * k;
-  xt.buffer_bytes = rows * k * 4;
-  xt.dtype = LC_F32;
-  xt.rank = 2;
-  xt.shape[0] = k;
-  xt.shape[1] = rows;
-  xt.strides[0] = 1;
-  xt.strides[1] = k;
-  lc_view dwv = matrix_view(p->dw[l], LC_F32, k, n, k * n * 4);
-  if ((st = lc_backend_gemm(p->ctx, p->comp(), &xt, &dpre, &dwv, 1.0f, 1.0f))) return st;
-  if (dx_out == nullptr) return LC_OK;
-  // dX[rows, k] = dpre [rows, n] @ W^T [n, k]  (:220)
-  lc_view wt{};
-  wt.data = p->master[l];
-  wt.buffer_bytes = k * n * 4;
-  wt.dtype = LC_F32;
-  wt.rank = 2;
-  wt.shape[0] = n;
-  wt.shape[1] = k;
-  wt.strides[0] = 1;
-  wt.strides[1] = n;
-  lc_view dx = matrix_view(dx_out, LC_F32, rows, k, rows * k * 4);
-  return lc_backend_gemm(p->ctx, p->comp(), &dpre, &wt, &dx, 1.0f, 0.0f);
+// The stage's backward of one microbatch in the reference's order (crates/pipeline/src/lib.rs:
+// 204-227): for l = count-1 .. 0, dpre = act'(pre[l]) * g, dW[l] += x^T dpre (beta = 1), g = dpre @
+// W^T for the layer below (sent to the previous stage after layer 0).  `g` is the gradient at the
+// stage's output (f32 [rows, n]).  GELU layers fold each act' into the product that makes its g
+// (the fused GELU-backward epilogue: the same bits as the product followed by gelu_backward), so
+// only the top layer's act' runs as its own kernel; dpre alternates between two scratch buffers.
+lc_status ref_backward_stage(lc_pipeline* p, uint64_t row0, uint64_t rows, const float* g) {
+  const bool gelu = p->cfg.activation == 0;
+  float* bufs[2] = {(float*)p->dbuf, (float*)p->dbuf2};
+  int cur = 0;
+  lc_status st = LC_OK;
+  {
+    const uint64_t l = p->count - 1, n = p->wout(l);
+    lc_view pre = matrix_view(p->pre[l] + row0 * n, LC_F32, rows, n, rows * n * 4);
+    lc_view gv = matrix_view(const_cast<float*>(g), LC_F32, rows, n, rows * n * 4);
+    lc_view dpre = matrix_view(bufs[cur], LC_F32, rows, n, rows * n * 4);
+    st = gelu ? lc_gelu_backward(p->ctx, p->comp(), &pre, &gv, &dpre) : lc_relu_backward(p->ctx, p->comp(), &pre, &gv, &dpre);
+    if (st) return st;
+  }
+  for (uint64_t l = p->count; l-- > 0;) {
+    const uint64_t k = p->win(l), n = p->wout(l);
+    lc_view dpre = matrix_view(bufs[cur], LC_F32, rows, n, rows * n * 4);
+    // dW[k, n] += x^T [k, rows] @ dpre [rows, n]  (:218, beta = 1)
+    lc_view xt{};
+    xt.data = (float*)p->H[l] + row0 * k;
+    xt.buffer_bytes = rows * k * 4;
+    xt.dtype = LC_F32;
+    xt.rank = 2;
+    xt.shape[0] = k;
+    xt.shape[1] = rows;
+    xt.strides[0] = 1;
+    xt.strides[1] = k;
+    lc_view dwv = matrix_view(p->dw[l], LC_F32, k, n, k * n * 4);
+    if ((st = lc_backend_gemm(p->ctx, p->comp(), &xt, &dpre, &dwv, 1.0f, 1.0f))) return st;
+    if (l == 0 && p->is_first()) break;  // the reference computes and discards this dx
+    // dX[rows, k] = dpre [rows, n] @ W^T [n, k]  (:220)
+    lc_view wt{};
+    wt.data = p->master[l];
+    wt.buffer_bytes = k * n * 4;
+    wt.dtype = LC_F32;
+    wt.rank = 2;
+    wt.shape[0] = n;
+    wt.shape[1] = k;
+    wt.strides[0] = 1;
+    wt.strides[1] = n;
+    if (l == 0) {
+      lc_view dx = matrix_view((float*)p->gsend + row0 * k, LC_F32, rows, k, rows * k * 4);
+      return lc_backend_gemm(p->ctx, p->comp(), &dpre, &wt, &dx, 1.0f, 0.0f);
+    }
+    // the layer below's dpre from this layer's dx
+    lc_view below_pre = matrix_view(p->pre[l - 1] + row0 * k, LC_F32, rows, k, rows * k * 4);
+    lc_view other = matrix_view(bufs[cur ^ 1], LC_F32, rows, k, rows * k * 4);
+    if (gelu) {
+      lc_epilogue e{};
+      e.kind = LC_EPI_GELU_BACKWARD;
+      e.aux = &below_pre;
+      st = lc_encode_gemm_fused(p->ctx, p->comp(), 1.0f, &dpre, &wt, 0.0f, &other, &e);
+      cur ^= 1;
+    } else {
+      // dx into the other buffer, then the layer below's dpre over this one (its last readers,
+      // the two products above, precede it on the stream)
+      st = lc_backend_gemm(p->ctx, p->comp(), &dpre, &wt, &other, 1.0f, 0.0f);
+      lc_view below = matrix_view(bufs[cur], LC_F32, rows, k, rows * k * 4);
+      if (!st) st = lc_relu_backward(p->ctx, p->comp(), &below_pre, &other, &below);
+    }
+    if (st) return st;
+  }
+  return LC_OK;
 }
 
 lc_status wait_step(lc_pipeline* p) {
@@ -959,17 +1002,7 @@ lc_status lc_pipeline_step(lc_pipeline* p, const float* x, const float* target_o
         }
         st = run_products(p, bs, probs);
       } else {
-        // g is consumed by the activation backward (into dbuf) before the dgrad GEMM writes dx,
-        // so dx can land in the buffer g came from (dbuf2) without any op reading and writing
-        // the same memory.
-        const float* g = g_ref;
-        for (uint64_t l = p->count; l-- > 0 && !st;) {
-          float* dx = nullptr;
-          if (l > 0) dx = (float*)p->dbuf2;
-          else if (!p->is_first()) dx = (float*)p->gsend + row0 * w0;
-          st = ref_backward(p, l, row0, mb, g, dx);
-          g = dx;
-        }
+        st = ref_backward_stage(p, row0, mb, g_ref);
       }
       if (st) break;
       if (p->trace) CU(cudaEventRecord(p->ev_t1[i], bs));

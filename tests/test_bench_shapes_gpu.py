@@ -288,3 +288,57 @@ def test_argmax_complex_ties_nans_and_extremes(ctx):
         big[4999] = np.float32([0.9, 0.3]) * m
         zb = as_complex(big)
         assert gpu_argmax_complex(ctx, zb, kind) == O.argmax_complex(zb, kind)
+
+
+# ------------------------------------------------------------------------------------------------
+# fused GELU epilogues (f32, the reference-mode pipeline's layers)
+# ------------------------------------------------------------------------------------------------
+
+@pytest.mark.parametrize("m,n,k", [(64, 512, 768), (200, 96, 130_001), (33, 1000, 64)])
+def test_gelu_epilogues_equal_the_unfused_sequence(ctx, m, n, k):
+    """gemm -> gelu and gemm -> gelu_backward (crates/pipeline/src/lib.rs:176-178, :211-220) as
+    one product each: bit-identical to lc_encode_gemm followed by the standalone lc_gelu /
+    lc_gelu_backward, and within tolerance of the oracle's gemm + gelu.  The long-K case splits."""
+    x = torch.from_numpy(data.uniform(60 + k, (m, k))).cuda()
+    w = torch.from_numpy(data.uniform(61 + k, (k, n)) * np.float32(k ** -0.5)).cuda()
+    pre_ref = torch.empty(m, n, device="cuda")
+    lb.encode_gemm(ctx, None, 1.0, x, w, 0.0, pre_ref)
+    act_ref = torch.empty_like(pre_ref)
+    lb.gelu(ctx, pre_ref, act_ref)
+    act = torch.empty_like(pre_ref)
+    pre = torch.empty_like(pre_ref)
+    lb.encode_gemm_fused(ctx, None, 1.0, x, w, 0.0, act, lb.EPI_GELU, aux2=pre)
+    ctx.sync()
+    assert torch.equal(pre.view(torch.int32), pre_ref.view(torch.int32))
+    assert torch.equal(act.view(torch.int32), act_ref.view(torch.int32))
+    cpu = np.zeros((m, n), np.float32)
+    O.gemm3(O.DT_F32, O.DT_F32, O.DT_F32, x.cpu().numpy(), w.cpu().numpy(), cpu, 1.0, 0.0, threads=THREADS)
+    assert normwise(act.cpu().numpy(), O.gelu(cpu)) <= 1e-4
+    # backward: dpre = gelu'(pre) * (g @ W^T), g the gradient arriving at the layer's output
+    g = torch.from_numpy(data.uniform(62 + k, (m, n))).cuda()
+    dx_ref = torch.empty(m, k, device="cuda")
+    pre_in = torch.from_numpy(data.normal(63 + k, (m, k))).cuda()  # the layer below's pre-activation
+    lb.encode_gemm(ctx, None, 1.0, g, w.t(), 0.0, dx_ref)
+    dpre_ref = torch.empty_like(dx_ref)
+    lb.gelu_backward(ctx, pre_in, dx_ref, dpre_ref)
+    dpre = torch.empty_like(dx_ref)
+    lb.encode_gemm_fused(ctx, None, 1.0, g, w.t(), 0.0, dpre, lb.EPI_GELU_BACKWARD, aux=pre_in)
+    ctx.sync()
+    assert torch.equal(dpre.view(torch.int32), dpre_ref.view(torch.int32))
+
+
+def test_fused_epilogue_argument_checks(ctx):
+    a = torch.zeros(64, 64, device="cuda")
+    b = torch.zeros(64, 64, device="cuda")
+    c = torch.zeros(64, 64, device="cuda")
+    with pytest.raises(lb.DtypeError):
+        lb.encode_gemm_fused(ctx, None, 1.0, a, b, 0.0, c, lb.EPI_RELU_MASK, aux=c)  # f32 inputs
+    with pytest.raises(lb.InvalidArgument):
+        lb.encode_gemm_fused(ctx, None, 1.0, a, b, 0.0, c, lb.EPI_GELU_BACKWARD)  # no pre-activation
+    with pytest.raises(lb.ShapeError):
+        lb.encode_gemm_fused(ctx, None, 1.0, a, b, 0.0, c, lb.EPI_GELU_BACKWARD, aux=torch.zeros(64, 32, device="cuda"))
+    with pytest.raises(lb.InvalidArgument):
+        lb.encode_gemm_fused(ctx, None, 1.0, a, b, 0.0, c, 9)
+    ab, bb = a.bfloat16(), b.bfloat16()
+    with pytest.raises(lb.DtypeError):
+        lb.encode_gemm_fused(ctx, None, 1.0, ab, bb, 0.0, c.bfloat16(), lb.EPI_GELU)
