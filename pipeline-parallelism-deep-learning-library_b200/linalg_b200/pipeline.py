@@ -142,7 +142,9 @@ def trace_summary(rec: np.ndarray, step_ms: float) -> dict:
     """Busy time of a stage (the union of its ops' compute intervals, forwards, backwards and
     weight updates) against its step time; the rest is time the stage had nothing it could run:
     the 1F1B fill and drain, and waits on transfers."""
-    iv = sorted((float(a), float(b)) for _, _, a, b in rec)
+    rec = [tuple(float(v) for v in r) for r in rec]
+    step_ms = float(step_ms)
+    iv = sorted((a, b) for _, _, a, b in rec)
     busy, cur_a, cur_b = 0.0, None, None
     for a, b in iv:
         if cur_b is None or a > cur_b:
