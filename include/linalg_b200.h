@@ -119,7 +119,9 @@ lc_status lc_slice(const lc_view* v, const uint64_t* starts, const uint64_t* end
 /* ---- contraction (src/ops/contraction.rs:1024-1130) --------------------------------------- */
 
 /* C = alpha*A*B + beta*C over einsum labels (`encode_contract`, :1036-1048; `contract`,
- * :1053-1064).  f32 runs 3xTF32 on tcgen05, f16/bf16 run kind::f16 with f32 accumulation. */
+ * :1053-1064).  f32 runs 3xTF32 on tcgen05 and bf16 kind::f16 with f32 accumulation; f16 rounds
+ * each output once from a double-float dot, as the reference's op API does (:147-160, 829-836),
+ * reading the operands in place whatever their strides. */
 lc_status lc_encode_contract(lc_context* ctx, void* stream, float alpha, const lc_view* a,
                              const char* a_labels, const lc_view* b, const char* b_labels, float beta,
                              const lc_view* c, const char* c_labels);
@@ -186,7 +188,8 @@ lc_status lc_encode_gemm_noalloc(lc_context* ctx, void* stream, float alpha, con
 
 /* Plan summary, for tests and reports (src/ops/contraction.rs:664-675 `Plan`). */
 typedef struct lc_contract_plan {
-    int32_t kind;    /* 0 Empty, 1 Fill, 2 Tiled, 3 Split, 4 Staged (operand materialised first) */
+    int32_t kind;    /* 0 Empty, 1 Fill, 2 Tiled, 3 Split, 4 Staged (operand materialised first),
+                        5 General (f16: read in place, one rounding of a double-float dot) */
     int32_t splits;  /* split-K slices (1 when not split) */
     uint64_t batch, m, n, k;
     int32_t swap_ab; /* 1 when the kernel computes C^T = B^T A^T (skinny M) */

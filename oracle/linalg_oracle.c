@@ -758,3 +758,94 @@ float or_mlp_step(uint64_t layers, uint64_t d, uint64_t batch_total, uint64_t mb
     free(wb); free(dw); free(h); free(pre); free(yd); free(g); free(dpre);
     return loss;
 }
+
+/* ------------------------------------------------------------------------------------ */
+/* f16 contraction of the op API: shaders/contraction.metal:445-702 (`two_sum`, `two_prod`, */
+/* `dd_add`, `dd_mul`, `dd_to_half`, `store_dd`, `contract_general_f16`) and :733-755     */
+/* (`contract_scale_f16`).  Each output: a double-float (hi, lo) sum of the exact f16 x f16 */
+/* products in k order, times alpha, plus beta * C, rounded once to f16 (ties to even; an  */
+/* f16 overflow of hi is kept).  Non-finite values take plain f32 arithmetic.             */
+/* ------------------------------------------------------------------------------------ */
+static void dd_two_sum(float a, float b, float* s, float* e) {
+    *s = a + b;
+    float v = *s - a;
+    *e = (a - (*s - v)) + (b - v);
+}
+static void dd_two_prod(float a, float b, float* p, float* e) {
+    *p = a * b;
+    *e = fmaf(a, b, -*p);
+}
+static int fin3(float a, float b, float c) { return isfinite(a) && isfinite(b) && isfinite(c); }
+static void dd_add1(float* hi, float* lo, float x) {
+    if (!fin3(*hi, *lo, x)) { *hi = (*hi + x) + *lo; *lo = 0.0f; return; }
+    float s, e;
+    dd_two_sum(*hi, x, &s, &e);
+    e = e + *lo;
+    dd_two_sum(s, e, hi, lo);
+}
+static void dd_mul1(float* hi, float* lo, float s) {
+    if (!fin3(*hi, *lo, s)) { *hi = fmaf(s, *hi, s * *lo); *lo = 0.0f; return; }
+    float p1, e1, p2, e2;
+    dd_two_prod(s, *hi, &p1, &e1);
+    dd_two_prod(s, *lo, &p2, &e2);
+    *hi = p1; *lo = e1;
+    dd_add1(hi, lo, p2);
+    dd_add1(hi, lo, e2);
+}
+static uint16_t f16_step1(uint16_t b, int up) {
+    int neg = (b & 0x8000u) != 0;
+    if (up != neg) return (uint16_t)(b + 1);
+    if ((b & 0x7fffu) == 0) return up ? 0x0001 : 0x8001;
+    return (uint16_t)(b - 1);
+}
+uint16_t or_dd_to_f16(float hi, float lo) {
+    if (!isfinite(hi) || !isfinite(lo)) return or_f32_to_f16(hi + lo);
+    uint16_t z = or_f32_to_f16(hi);
+    if ((z & 0x7c00u) == 0x7c00u) return z;
+    float zf = or_f16_to_f32(z);
+    float r, rl;
+    dd_two_sum(hi - zf, lo, &r, &rl);
+    uint32_t mag = z & 0x7fffu;
+    float ulp = mag < 0x0400u ? u2f(0x33800000u) : u2f((uint32_t)((int)(mag >> 10) - 25 + 127) << 23);
+    uint32_t ex = (z >> 10) & 0x1fu;
+    int pow2 = (z & 0x03ffu) == 0 && ex >= 2;
+    float away = ulp * 0.5f, toward = pow2 ? ulp * 0.25f : away;
+    int neg = (z & 0x8000u) != 0, odd = z & 1u;
+    float up = neg ? toward : away, dn = neg ? away : toward;
+    if (r > up || (r == up && (rl > 0.0f || (rl == 0.0f && odd)))) return f16_step1(z, 1);
+    if (r < -dn || (r == -dn && (rl < 0.0f || (rl == 0.0f && odd)))) return f16_step1(z, 0);
+    return z;
+}
+
+/* C[m x n] (f16 bits, row stride c_rs) = alpha * A B + beta * C; A element (i, k) at
+ * a[i*a_rs + k*a_cs], B element (k, j) at b[k*b_rs + j*b_cs].  K = 0 or alpha = 0 with beta
+ * != 0 is the once-rounded scale; beta == 0 with alpha == 0 writes +0. */
+void or_contract_f16(uint64_t m, uint64_t n, uint64_t k, float alpha, float beta,
+                     const uint16_t* a, uint64_t a_rs, uint64_t a_cs, const uint16_t* b, uint64_t b_rs,
+                     uint64_t b_cs, uint16_t* c, uint64_t c_rs) {
+    for (uint64_t i = 0; i < m; i++)
+        for (uint64_t j = 0; j < n; j++) {
+            uint16_t* cp = c + i * c_rs + j;
+            if (alpha == 0.0f || k == 0) {
+                if (beta == 0.0f) { *cp = 0; continue; }
+                float cv = or_f16_to_f32(*cp), hi = 0.0f, lo = 0.0f;
+                if (isfinite(beta) && isfinite(cv)) dd_two_prod(beta, cv, &hi, &lo);
+                if (!isfinite(beta) || !isfinite(cv) || !isfinite(hi) || !isfinite(lo)) *cp = or_f32_to_f16(beta * cv);
+                else *cp = or_dd_to_f16(hi, lo);
+                continue;
+            }
+            float hi = 0.0f, lo = 0.0f;
+            for (uint64_t kk = 0; kk < k; kk++)
+                dd_add1(&hi, &lo, or_f16_to_f32(a[i * a_rs + kk * a_cs]) * or_f16_to_f32(b[kk * b_rs + j * b_cs]));
+            dd_mul1(&hi, &lo, alpha);
+            if (beta != 0.0f) {
+                float cv = or_f16_to_f32(*cp);
+                if (!fin3(hi, lo, cv)) { *cp = or_f32_to_f16((hi + lo) + beta * cv); continue; }
+                float bh, bl;
+                dd_two_prod(beta, cv, &bh, &bl);
+                dd_add1(&hi, &lo, bh);
+                dd_add1(&hi, &lo, bl);
+            }
+            *cp = or_dd_to_f16(hi, lo);
+        }
+}

@@ -60,6 +60,8 @@ def lib() -> C.CDLL:
             "or_argmax": (_u64, [_ptr, _u64, _u64]),
             "or_argmax_rows": (None, [_ptr, _u64, _u64, _u64, _u64, _ptr]),
             "or_mag32": (_f32, [_f32, _f32, C.c_int]),
+            "or_dd_to_f16": (C.c_uint16, [_f32, _f32]),
+            "or_contract_f16": (None, [_u64, _u64, _u64, _f32, _f32, _ptr, _u64, _u64, _ptr, _u64, _u64, _ptr, _u64]),
             "or_argmax_complex": (_u64, [_ptr, _u64, _u64, C.c_int]),
             "or_sqrt": (None, [_ptr, _ptr, _u64]),
             "or_reciprocal": (None, [_ptr, _ptr, _u64]),
@@ -267,6 +269,23 @@ def argmax(x: np.ndarray, stride: int = 1, n: int | None = None) -> int:
     x = np.ascontiguousarray(x, dtype=np.float32)
     n = x.size if n is None else n
     return int(lib().or_argmax(_p(x), n, stride))
+
+
+def contract_f16(a_bits: np.ndarray, b_bits: np.ndarray, c_bits: np.ndarray, alpha: float, beta: float,
+                 a_strides=None, b_strides=None, k: int | None = None) -> np.ndarray:
+    """The op API's f16 product (shaders/contraction.metal:445-755): every output rounded once
+    from a double-float dot.  Arrays hold f16 bits (uint16); c_bits [m, n] row-major is updated."""
+    a = np.ascontiguousarray(a_bits, dtype=np.uint16)
+    b = np.ascontiguousarray(b_bits, dtype=np.uint16)
+    assert c_bits.dtype == np.uint16 and c_bits.flags.c_contiguous
+    m, n = c_bits.shape
+    if k is None:
+        k = a.shape[1] if a_strides is None else a.shape[0]
+    a_rs, a_cs = (k, 1) if a_strides is None else a_strides
+    b_rs, b_cs = (n, 1) if b_strides is None else b_strides
+    lib().or_contract_f16(m, n, k, float(np.float32(alpha)), float(np.float32(beta)), _p(a), a_rs, a_cs, _p(b), b_rs,
+                          b_cs, _p(c_bits), n)
+    return c_bits
 
 
 MAG_L1, MAG_HYPOT = 0, 1

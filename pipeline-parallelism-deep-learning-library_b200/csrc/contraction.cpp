@@ -27,6 +27,7 @@
 #include <vector>
 
 #include "gemm.h"
+#include "general_f16.h"
 #include "internal.h"
 
 namespace {
@@ -303,6 +304,10 @@ void dense_strides(const std::vector<uint64_t>& shape, size_t nb, size_t nr, uin
 struct Plan {
   int kind = 0;  // 0 empty, 1 fill, 2 gemm
   GemmProblem prob;
+  // f16 with the op API's rounding: the product (or the fill) runs on general_f16_run, reading
+  // the operands in place through the groups' strides
+  bool f16_general = false;
+  Groups groups;
   bool stage_a = false, stage_b = false, stage_c = false;
   // staging geometry
   std::vector<uint64_t> a_shape, a_src, b_shape, b_src, c_shape, c_src;
@@ -321,6 +326,7 @@ lc_status plan_groups(lc_context* ctx, const lc_view& a, const lc_view& b, const
   plan->bv = &b;
   plan->cv = &c;
   GemmProblem& pr = plan->prob;
+  plan->groups = g;
   pr.m = mt;
   pr.n = nt;
   pr.k = kt;
@@ -457,6 +463,38 @@ lc_status execute(lc_context* ctx, cudaStream_t s, Plan& plan, lc_contract_plan*
     report->k = pr.k;
   }
   if (plan.kind == 0) return LC_OK;
+  if (plan.f16_general) {
+    if (report && plan.kind == 2) report->kind = 5;
+    if (dry_run) return LC_OK;
+    GenParams gp;
+    gp.m = pr.m;
+    gp.n = pr.n;
+    gp.k = pr.k;
+    gp.batch = pr.batch;
+    auto fill_group = [](const std::vector<Axis>& axes, GenGroup* out) {
+      out->n = 0;
+      for (const Axis& ax : axes) {
+        out->ext[out->n] = ax.extent;
+        out->st[0][out->n] = (int64_t)ax.sa;
+        out->st[1][out->n] = (int64_t)ax.sb;
+        out->st[2][out->n] = (int64_t)ax.sc;
+        out->n++;
+      }
+    };
+    fill_group(plan.groups.batch, &gp.gb);
+    fill_group(plan.groups.m, &gp.gm);
+    fill_group(plan.groups.n, &gp.gn);
+    fill_group(plan.groups.k, &gp.gk);
+    gp.a = static_cast<const uint16_t*>(plan.av->data);
+    gp.b = static_cast<const uint16_t*>(plan.bv->data);
+    gp.c = static_cast<uint16_t*>(plan.cv->data);
+    gp.a_off = plan.av->offset;
+    gp.b_off = plan.bv->offset;
+    gp.c_off = plan.cv->offset;
+    gp.alpha = pr.alpha;
+    gp.beta = pr.beta;
+    return general_f16_run(ctx, s, gp, plan.kind == 1);
+  }
   if (dry_run && plan.kind == 1) return LC_OK;
   if (dry_run) {
     GemmProblem q = pr;
@@ -549,11 +587,14 @@ lc_status contract_impl(lc_context* ctx, void* stream, float alpha, const lc_vie
   if ((st = groups_from_labels(*a, pa, *b, pb, *c, pc, &g))) return st;
   Plan plan;
   if ((st = plan_groups(ctx, *a, *b, *c, g, alpha, beta, &plan))) return st;
+  plan.f16_general = a->dtype == LC_F16;
   return execute(ctx, stream_of(ctx, stream), plan, report, dry_run);
 }
 
+// op_api: the op API's `gemm` (f16 rounds once from a double-float dot); otherwise the Backend
+// slot's gemm, whose f16 products run on the tensor cores with f32 accumulation.
 lc_status gemm_impl(lc_context* ctx, void* stream, float alpha, const lc_view* a, const lc_view* b, float beta,
-                    const lc_view* c) {
+                    const lc_view* c, bool op_api) {
   if (ctx == nullptr) return fail(LC_ERR_INVALID_ARGUMENT, "null context");
   lc_status st = prepare(a, b, c);
   if (st) return st;
@@ -561,6 +602,7 @@ lc_status gemm_impl(lc_context* ctx, void* stream, float alpha, const lc_view* a
   if ((st = groups_from_gemm(*a, *b, *c, &g))) return st;
   Plan plan;
   if ((st = plan_groups(ctx, *a, *b, *c, g, alpha, beta, &plan))) return st;
+  plan.f16_general = op_api && a->dtype == LC_F16;
   return execute(ctx, stream_of(ctx, stream), plan, nullptr, false);
 }
 
@@ -666,7 +708,8 @@ lc_status gemm_fixed_scratch(lc_context* ctx, void* stream, float alpha, const l
   if ((st = groups_from_gemm(*a, *b, *c, &g))) return st;
   Plan plan;
   if ((st = plan_groups(ctx, *a, *b, *c, g, alpha, beta, &plan))) return st;
-  if (plan.stage_a || plan.stage_b || plan.stage_c)
+  plan.f16_general = a->dtype == LC_F16;  // lc_encode_gemm's semantics; it needs no scratch
+  if (!plan.f16_general && (plan.stage_a || plan.stage_b || plan.stage_c))
     return fail(LC_ERR_INVALID_ARGUMENT,
                 "this product needs staging copies of its operands, which the allocation-free entry point "
                 "cannot hold: pass operands with a unit stride and 16-byte aligned starts and strides");
@@ -702,7 +745,7 @@ lc_status lc_plan_contract(lc_context* ctx, float alpha, const lc_view* a, const
 
 lc_status lc_encode_gemm(lc_context* ctx, void* stream, float alpha, const lc_view* a, const lc_view* b, float beta,
                          const lc_view* c) {
-  return gemm_impl(ctx, stream, alpha, a, b, beta, c);
+  return gemm_impl(ctx, stream, alpha, a, b, beta, c, true);
 }
 
 lc_status lc_encode_gemm_fused(lc_context* ctx, void* stream, float alpha, const lc_view* a, const lc_view* b,
@@ -746,7 +789,7 @@ lc_status lc_backend_gemm(lc_context* ctx, void* stream, const lc_view* a, const
     if (!range_ok(*c)) return fail(LC_ERR_SHAPE, "C buffer too short");
     if (alpha != 0.0f && k > 0 && (!range_ok(*a) || !range_ok(*b))) return fail(LC_ERR_SHAPE, "operand buffer too short");
   }
-  return gemm_impl(ctx, stream, alpha, a, b, beta, c);
+  return gemm_impl(ctx, stream, alpha, a, b, beta, c, false);
 }
 
 }  // extern "C"

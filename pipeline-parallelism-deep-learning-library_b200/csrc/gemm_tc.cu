@@ -59,6 +59,7 @@ struct KParams {
   int32_t fixup;    // 1: the last-arriving warp reduces in the kernel; 0: a separate reduce kernel does
   int32_t split_minor;  // unit u = tile * splits + split (CTA pairs); else u = split * tiles + tile
   int32_t a_once, b_once;  // the operand is read by exactly one CTA (one tile column / row): evict first
+  int32_t prefetch;  // k-tiles of the once-read A operand requested into L2 ahead of the ring (0: none)
   int32_t vec;      // C's columns contiguous and every row start 16-byte aligned (C, aux and aux2)
   int32_t tvec;     // C's rows contiguous instead (swapped products), runs of 8 rows 16-byte aligned
   int* err;
@@ -75,6 +76,7 @@ struct KParams {
 };
 
 constexpr int kSmemMax = 232448;  // dynamic shared memory a CTA may opt in to on sm_100
+constexpr int kPrefetchTiles = 0;  // default L2 prefetch distance of CTA-pair products, in k-tiles
 
 template <int BN, bool TF32X3, bool PAIR = false, bool TWO_SM = false>
 struct Cfg {
@@ -851,7 +853,20 @@ __device__ __forceinline__ void gemm_body(const Src& src) {
           const int32_t kb = split * p.kt_per_split;
           const int32_t ke = min(kb + p.kt_per_split, p.k_tiles);
           const int32_t a_row0 = tile_row0(tm);
+          // The streamed operand's DRAM reads run `prefetch` k-tiles ahead through L2, beyond the
+          // few the shared-memory ring holds; its ring loads then find the tiles in L2.
+          auto prefetch_a = [&](int32_t kt) {
+            if (!p.a_mn) {
+              lcd::tma_prefetch_l2_3d(ta, kt * C::BK, a_row0, b);
+            } else {
+#pragma unroll
+              for (int j = 0; j < kBM / C::EPR; j++) lcd::tma_prefetch_l2_3d(ta, a_row0 + j * C::EPR, kt * C::BK, b);
+            }
+          };
+          if (p.prefetch > 0 && p.a_once)
+            for (int32_t kt = kb + C::STAGES; kt < min(ke, kb + p.prefetch); kt++) prefetch_a(kt);
           for (int32_t kt = kb; kt < ke; kt++) {
+            if (p.prefetch > 0 && p.a_once && kt + p.prefetch < ke) prefetch_a(kt + p.prefetch);
             // every slot holds an A tile waiting for its B: open the gate before reusing one
             if (!open && npend == C::STAGES && !release()) {
               ok = false;
@@ -1921,6 +1936,13 @@ lc_status plan_gemm(lc_context* ctx, const lc::GemmProblem& pr, lc_contract_plan
   }();
   p.a_once = (tiles_n == 1 && !env_no_hint) ? 1 : 0;
   p.b_once = (tiles_m_eff == 1 && !env_no_hint) ? 1 : 0;
+  static const int env_prefetch = [] {
+    const char* e = getenv("LC_GEMM_PREFETCH");  // tuning override: k-tiles of L2 prefetch ahead (0 = off)
+    return e ? atoi(e) : -1;
+  }();
+  // L2 prefetch of the streamed operand (16-bit CTA-pair products, whose A is the weight matrix
+  // of the pipeline's skinny and grouped products)
+  p.prefetch = (pair && !tf32x3) ? (env_prefetch >= 0 ? env_prefetch : kPrefetchTiles) : 0;
   p.a_mn = a_mn;
   p.b_mn = b_mn;
   const uint32_t fmt = tf32x3 ? 2u : (pr.in_dtype == LC_BF16 ? 1u : 0u);

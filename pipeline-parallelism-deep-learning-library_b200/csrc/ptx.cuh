@@ -183,6 +183,15 @@ __device__ __forceinline__ void tma_load_3d(void* smem_dst, const void* desc, ui
 
 // L2 policy for data read exactly once (a streamed weight matrix): evicted first, so it does not
 // push reused operands, partial sums or the kernel's own code out of L2.
+// Brings one box of a tiled tensor map into L2 (no shared memory, no barrier): used to run the
+// DRAM reads of a streamed operand further ahead than the shared-memory ring reaches.
+__device__ __forceinline__ void tma_prefetch_l2_3d(const void* desc, int32_t c0, int32_t c1, int32_t c2) {
+  asm volatile("cp.async.bulk.prefetch.tensor.3d.L2.global.tile [%0, {%1, %2, %3}];" ::"l"(
+                   reinterpret_cast<uint64_t>(desc)),
+               "r"(c0), "r"(c1), "r"(c2)
+               : "memory");
+}
+
 __device__ __forceinline__ uint64_t policy_evict_first() {
   uint64_t p;
   asm volatile("createpolicy.fractional.L2::evict_first.b64 %0, 1.0;" : "=l"(p));

@@ -353,7 +353,7 @@ def plan_contract(ctx: Context, alpha, a, b, beta, c) -> dict:
     p = lc_contract_plan()
     check(load().lc_plan_contract(ctx.h if ctx is not None else None, float(alpha), av.ref(), al.encode(), bv.ref(), bl.encode(), float(beta),
                                   cv.ref(), cl.encode(), C.byref(p)))
-    kinds = {0: "Empty", 1: "Fill", 2: "Tiled", 3: "Split", 4: "Staged"}
+    kinds = {0: "Empty", 1: "Fill", 2: "Tiled", 3: "Split", 4: "Staged", 5: "General"}
     return {"kind": kinds[p.kind], "splits": p.splits, "batch": p.batch, "m": p.m, "n": p.n, "k": p.k,
             "swap_ab": bool(p.swap_ab), "a_major": "MN" if p.a_major else "K", "b_major": "MN" if p.b_major else "K"}
 

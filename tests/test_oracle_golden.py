@@ -385,3 +385,26 @@ def test_mlp_step_decreases_loss_and_is_thread_invariant():
     assert l1 == l2 and (m1.view(np.uint32) == m2.view(np.uint32)).all()
     l3 = O.mlp_step(m1, x, t, mb, 0.5, threads=1)
     assert l3 < l1
+
+
+def test_f16_scale_rounds_once_golden():
+    g = G["contract_f16_scale"]
+    for cin, cout in g["cases"]:
+        c = np.array([[int(cin, 16)]], np.uint16)
+        O.contract_f16(np.zeros((1, 0), np.uint16), np.zeros((0, 1), np.uint16), c, 1.0, g["beta"], k=0)
+        assert int(c[0, 0]) == int(cout, 16), (cin, hex(int(c[0, 0])))
+
+
+def test_f16_contraction_is_the_correctly_rounded_dot():
+    """A double-float dot of exact f16 products, rounded once, is the correctly rounded f16 of
+    the exact sum (the f64 sum of these products is exact to far below an f16 half-ulp), which is
+    what the reference's gate expects of f16 outputs (tests/contraction_test.rs:1-13)."""
+    rng = np.random.default_rng(16)
+    for m, n, k, alpha, beta in ((7, 9, 33, 1.0, 0.0), (16, 5, 1000, -0.5, 0.0), (4, 4, 257, 2.0, 1.0)):
+        a = rng.standard_normal((m, k)).astype(np.float16)
+        b = rng.standard_normal((k, n)).astype(np.float16)
+        c0 = rng.standard_normal((m, n)).astype(np.float16)
+        c = c0.view(np.uint16).copy()
+        O.contract_f16(a.view(np.uint16), b.view(np.uint16), c, alpha, beta)
+        exact = alpha * (a.astype(np.float64) @ b.astype(np.float64)) + beta * c0.astype(np.float64)
+        assert np.array_equal(c, exact.astype(np.float16).view(np.uint16)), (m, n, k)
