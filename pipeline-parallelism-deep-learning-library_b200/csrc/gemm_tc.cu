@@ -117,7 +117,7 @@ struct Cfg {
   static_assert(SMEM <= kSmemMax, "shared memory budget");
   static_assert(!PAIR || (!TF32X3 && BN <= 256), "CTA pairs: 16-bit inputs, BN <= 256");
   static_assert(!PAIR || STAGES >= 4, "CTA pairs keep at least 4 stages in flight");
-  static_assert(!TWO_SM || (!TF32X3 && !PAIR && BN == 256), "2-SM products: 16-bit inputs, BN = 256");
+  static_assert(!TWO_SM || (!TF32X3 && BN == 256), "2-SM products: 16-bit inputs, BN = 256");
 };
 
 __device__ __forceinline__ void unit_coords(const KParams& p, int32_t u, int32_t* b, int32_t* split, int32_t* tm,
@@ -697,8 +697,9 @@ __device__ __forceinline__ bool wait_counter(const int* counter, int target, int
   return true;
 }
 
-// TWO_SM: the 256-row tile of a unit is computed by a cluster of 2 CTAs with cta_group::2 MMAs
-// (rows 128 * rank .. + 127 of the tile live in CTA rank's TMEM); a unit is one output tile and
+// TWO_SM: the 256-row tile of a unit is computed by a pair of CTAs with cta_group::2 MMAs
+// (rows 128 * (rank & 1) .. + 127 of the tile live in that CTA's TMEM, the even CTA issues the
+// MMAs); a unit is one output tile and
 // the pair walks the units together.
 template <int BN, bool TF32X3, int EPI, bool PAIR, class Src, bool TWO_SM = false>
 __device__ __forceinline__ void gemm_body(const Src& src) {
@@ -772,11 +773,20 @@ __device__ __forceinline__ void gemm_body(const Src& src) {
   // both CTAs of a pair have initialised their barriers before either arrives on the other's
   if constexpr (PAIR || TWO_SM) lcd::cluster_sync();
   const uint32_t rank = (PAIR || TWO_SM) ? lcd::cluster_ctarank() : 0u;
-  // the units this CTA walks: every CTA on its own, or (TWO_SM) the pair together
-  const int32_t u_first = TWO_SM ? (int32_t)(blockIdx.x >> 1) : (int32_t)blockIdx.x;
-  const int32_t u_step = TWO_SM ? (int32_t)(gridDim.x >> 1) : (int32_t)gridDim.x;
+  // QUAD (PAIR and TWO_SM): a cluster of 4 is two 2-SM pairs, pair kh = rank >> 1 computing K
+  // half kh of the same 256-row tile; the pairs exchange partials as PAIR CTAs do.
+  constexpr bool QUAD = PAIR && TWO_SM;
+  const uint32_t leader = rank & ~1u;                    // the even CTA of this CTA's 2-SM pair
+  const bool is_leader = !TWO_SM || (rank & 1u) == 0u;  // issues the MMAs and arms the stages
+  const uint32_t kh = QUAD ? rank >> 1 : rank;           // PAIR: the K half this CTA (pair) sums
+  // the units this CTA walks: every CTA on its own, (TWO_SM) the pair together, or (QUAD) the pair
+  // with the other pair of its cluster on the other split of the same tile
+  const int32_t u_first = QUAD     ? (int32_t)(((blockIdx.x >> 2) << 1) | (rank >> 1))
+                          : TWO_SM ? (int32_t)(blockIdx.x >> 1)
+                                   : (int32_t)blockIdx.x;
+  const int32_t u_step = QUAD ? (int32_t)((gridDim.x >> 2) << 1) : TWO_SM ? (int32_t)(gridDim.x >> 1) : (int32_t)gridDim.x;
   // first C row of a unit's tile row tm held by this CTA
-  auto tile_row0 = [&](int32_t tm) -> int32_t { return TWO_SM ? tm * 256 + (int32_t)rank * 128 : tm * kBM; };
+  auto tile_row0 = [&](int32_t tm) -> int32_t { return TWO_SM ? tm * 256 + (int32_t)(rank & 1u) * 128 : tm * kBM; };
   // Programmatic dependent launch: the next kernel on the stream may start its own set-up now.
   // Everything below that reads or writes global memory first waits for the previous kernel.
   lcd::griddep_launch_dependents();
@@ -820,7 +830,7 @@ __device__ __forceinline__ void gemm_body(const Src& src) {
         auto load = [&](int st, void* dst, const CUtensorMap* map, int32_t c0, int32_t c1, int32_t b, bool hint) {
           if constexpr (TWO_SM) {
             // bytes count on the leader's barrier for this stage
-            lcd::tma_load_3d_2sm(dst, map, lcd::leader_addr(lcd::smem_u32(&full[st])), c0, c1, b,
+            lcd::tma_load_3d_2sm(dst, map, lcd::rank_addr(lcd::smem_u32(&full[st]), leader), c0, c1, b,
                                  hint ? once : (EPI == 2 ? keep : normal));
           } else {
             if (hint) lcd::tma_load_3d_hint(dst, map, &full[st], c0, c1, b, once);
@@ -830,7 +840,7 @@ __device__ __forceinline__ void gemm_body(const Src& src) {
         };
         // this CTA's rows of the B^T tile: all BN, or (TWO_SM) its half
         constexpr int kBRows = TWO_SM ? BN / 2 : BN;
-        const int32_t b_row_off = TWO_SM ? (int32_t)rank * kBRows : 0;
+        const int32_t b_row_off = TWO_SM ? (int32_t)(rank & 1u) * kBRows : 0;
         auto load_b = [&](int st, int32_t k0, int32_t tn, int32_t b) {
           if (!p.b_mn) {
             load(st, b_hi(st), tb, k0, tn * BN + b_row_off, b, p.b_once);
@@ -878,7 +888,7 @@ __device__ __forceinline__ void gemm_body(const Src& src) {
             }
             // TWO_SM: only the leader arms the stage (with both CTAs' bytes); the peer's loads
             // may land first, which an mbarrier allows while its arrival is still pending
-            if (!TWO_SM || rank == 0) lcd::mbar_arrive_expect_tx(&full[s], kStageTx);
+            if (is_leader) lcd::mbar_arrive_expect_tx(&full[s], kStageTx);
             const int32_t k0 = kt * C::BK;
             if (!p.a_mn) {
               load(s, a_hi(s), ta, k0, a_row0, b, p.a_once);
@@ -910,12 +920,12 @@ __device__ __forceinline__ void gemm_body(const Src& src) {
       // never leave a bulk copy in flight into shared memory that is about to be released (the
       // 2-SM peer's copies complete on the leader's barriers; the closing cluster barrier covers
       // them, as the leader waits here first)
-      if (!TWO_SM || rank == 0)
+      if (is_leader)
         for (int t = 0; t < C::STAGES; t++)
           if (filled & (1u << t)) lcd::mbar_wait(&full[t], (last_par >> t) & 1u, err);
     }
   } else if (warp == 1) {
-    if (lane == 0 && (!TWO_SM || rank == 0)) {
+    if (lane == 0 && is_leader) {
       // ---------------- MMA issuer (TWO_SM: the leader, for both CTAs) ----------------
       // The accumulator is handed to the epilogue every KC k-tiles (a "chunk"): once per unit for
       // 16-bit inputs, every kChunkTiles k-tiles for 3xTF32, whose long sums the epilogue then
@@ -982,7 +992,7 @@ __device__ __forceinline__ void gemm_body(const Src& src) {
               lcd::umma_f16(d_tmem, da, db, p.idesc, accum);
             }
           }
-          if constexpr (TWO_SM) lcd::umma_commit_2sm_both(&empty[s]);  // frees the stage in both CTAs
+          if constexpr (TWO_SM) lcd::umma_commit_2sm_pair(&empty[s], leader);  // frees the stage in both CTAs
           else lcd::umma_commit(&empty[s]);
           if (++s == C::STAGES) {
             s = 0;
@@ -990,7 +1000,7 @@ __device__ __forceinline__ void gemm_body(const Src& src) {
           }
         }
         if (!ok) break;
-        if constexpr (TWO_SM) lcd::umma_commit_2sm_both(&tfull[acc]);
+        if constexpr (TWO_SM) lcd::umma_commit_2sm_pair(&tfull[acc], leader);
         else lcd::umma_commit(&tfull[acc]);
         }
       }
@@ -1115,7 +1125,7 @@ __device__ __forceinline__ void gemm_body(const Src& src) {
         lcd::tc_fence_after();
         const int row = q * 32 + lane;
         const uint32_t sw = (uint32_t)(row & 7);
-        const uint32_t peer = rank ^ 1u;
+        const uint32_t peer = QUAD ? rank ^ 2u : rank ^ 1u;  // the CTA with the other K half of these rows
 #pragma unroll 1
         for (int rd = 0; ok && rd < C::EXCH_ROUNDS; rd++, xr++) {
         // (1) this round's columns of the peer's half, once the peer has consumed what this CTA
@@ -1129,7 +1139,7 @@ __device__ __forceinline__ void gemm_body(const Src& src) {
           uint32_t r[GR][32];
 #pragma unroll
           for (int gl = 0; gl < GR; gl++)
-            lcd::tmem_ld_32x32b_x32(lane_base + acc * BN + (peer * GH + rd * GR + gl) * 32, r[gl]);
+            lcd::tmem_ld_32x32b_x32(lane_base + acc * BN + ((kh ^ 1u) * GH + rd * GR + gl) * 32, r[gl]);
           lcd::tmem_ld_wait();
 #pragma unroll
           for (int gl = 0; gl < GR; gl++) {
@@ -1151,7 +1161,7 @@ __device__ __forceinline__ void gemm_body(const Src& src) {
         const float* src = recv + row * HB;
 #pragma unroll 1
         for (int gl = 0; gl < GR; gl++) {
-          const int g = (int)rank * GH + rd * GR + gl;
+          const int g = (int)kh * GH + rd * GR + gl;
           uint32_t r[32];
           lcd::tmem_ld_32x32b_x32(lane_base + acc * BN + g * 32, r);
           lcd::tmem_ld_wait();
@@ -1164,7 +1174,7 @@ __device__ __forceinline__ void gemm_body(const Src& src) {
 #pragma unroll
             for (int e = 0; e < 4; e++) {
               const float mine = __uint_as_float(r[4 * k + e]);
-              v[4 * k + e] = rank == 0 ? __fadd_rn(__fadd_rn(0.0f, mine), in[e]) : __fadd_rn(__fadd_rn(0.0f, in[e]), mine);
+              v[4 * k + e] = kh == 0 ? __fadd_rn(__fadd_rn(0.0f, mine), in[e]) : __fadd_rn(__fadd_rn(0.0f, in[e]), mine);
             }
           }
           const int32_t n0 = tn * BN + g * 32;
@@ -1178,7 +1188,7 @@ __device__ __forceinline__ void gemm_body(const Src& src) {
 #pragma unroll
             for (int j = 0; j < 32; j++) slot[j * HB + (lane ^ (4 * (j & 7)))] = v[j];
             __syncwarp();
-            const int32_t mw = tm * kBM + q * 32;
+            const int32_t mw = tile_row0(tm) + q * 32;
             store_cols<EPI>(p, slot, HB, p.c_off + (int64_t)b * p.c_bs + mw + (int64_t)n0 * p.c_ns,
                             min(32, p.M - mw), cnt);
           } else if (m < p.M && cnt > 0) {
@@ -1190,7 +1200,11 @@ __device__ __forceinline__ void gemm_body(const Src& src) {
         if (!ok) break;
         lcd::tc_fence_before();
         __syncwarp();
-        if (lane == 0) lcd::mbar_arrive(&tempty[acc]);
+        // QUAD: the pair's leader refills both CTAs' accumulators, so both release on its barrier
+        if (lane == 0) {
+          if (!is_leader) lcd::mbar_arrive_remote(lcd::rank_addr(lcd::smem_u32(&tempty[acc]), leader));
+          else lcd::mbar_arrive(&tempty[acc]);
+        }
         h++;
       } else {
         const int acc = h & 1;
@@ -1252,7 +1266,7 @@ __device__ __forceinline__ void gemm_body(const Src& src) {
         // arrivals per unit from the peer held the leader's next MMAs back by 2-4 us)
         __syncwarp();
         if (lane == 0) {
-          if (TWO_SM && rank == 1) lcd::mbar_arrive_remote(lcd::leader_addr(lcd::smem_u32(&tempty[acc])));
+          if (!is_leader) lcd::mbar_arrive_remote(lcd::rank_addr(lcd::smem_u32(&tempty[acc]), leader));
           else lcd::mbar_arrive(&tempty[acc]);
         }
         h++;
@@ -1389,6 +1403,15 @@ __global__ void __launch_bounds__(Cfg<256, false, false, true>::THREADS, 1)
     gemm_2sm_kernel(const __grid_constant__ CUtensorMap tma_a, const __grid_constant__ CUtensorMap tma_b,
                     const __grid_constant__ KParams p) {
   gemm_body<256, false, EPI, false, OneProduct, true>(OneProduct{&tma_a, &tma_b, &p});
+}
+
+// 256 x 256 tiles over a cluster of 4: two CTA pairs with cta_group::2 MMAs, each summing one half
+// of K, exchanging partials through distributed shared memory (16-bit inputs, 2-way split).
+template <int EPI>
+__global__ void __launch_bounds__(Cfg<256, false, true, true>::THREADS, 1)
+    gemm_quad_kernel(const __grid_constant__ CUtensorMap tma_a, const __grid_constant__ CUtensorMap tma_b,
+                     const __grid_constant__ KParams p) {
+  gemm_body<256, false, EPI, true, OneProduct, true>(OneProduct{&tma_a, &tma_b, &p});
 }
 
 // A chain of skinny products (BN = 64, 16-bit inputs, CTA pairs): the pipeline's layer loop of
@@ -1731,6 +1754,63 @@ lc_status launch_2sm(lc_context* ctx, cudaStream_t s, const CUtensorMap& ta, con
   return LC_OK;
 }
 
+template <int EPI>
+cudaLaunchConfig_t launch_config_quad(cudaStream_t s, int grid, cudaLaunchAttribute (&at)[2]) {
+  cudaLaunchConfig_t cfg = launch_config_2sm<EPI>(s, grid, at);
+  cfg.dynamicSmemBytes = Cfg<256, false, true, true>::SMEM;
+  at[1].val.clusterDim.x = 4;
+  return cfg;
+}
+
+template <int EPI>
+lc_status prepare_quad(lc_context* ctx) {
+  static bool attr_set[64] = {false};
+  if (!attr_set[ctx->device % 64]) {
+    cudaError_t e = cudaFuncSetAttribute(gemm_quad_kernel<EPI>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                         Cfg<256, false, true, true>::SMEM);
+    if (e != cudaSuccess) return lc::cuda_fail(e, "cudaFuncSetAttribute(gemm quad)");
+    attr_set[ctx->device % 64] = true;
+  }
+  return LC_OK;
+}
+
+// How many clusters of 4 fit on the device at once (0 when they cannot launch).
+template <int EPI>
+int capacity_quad(lc_context* ctx) {
+  static int cap[64];
+  static bool known[64] = {false};
+  const int d = ctx->device % 64;
+  if (!known[d]) {
+    int n = 0;
+    if (prepare_quad<EPI>(ctx) == LC_OK) {
+      cudaLaunchAttribute at[2];
+      cudaLaunchConfig_t cfg = launch_config_quad<EPI>(nullptr, 4, at);
+      if (cudaOccupancyMaxActiveClusters(&n, gemm_quad_kernel<EPI>, &cfg) != cudaSuccess) {
+        cudaGetLastError();
+        n = 0;
+      }
+    }
+    cap[d] = n;
+    known[d] = true;
+  }
+  return cap[d];
+}
+
+template <int EPI>
+lc_status launch_quad(lc_context* ctx, cudaStream_t s, const CUtensorMap& ta, const CUtensorMap& tb, const KParams& p,
+                      int grid) {
+  lc_status st = prepare_quad<EPI>(ctx);
+  if (st) return st;
+  cudaLaunchAttribute at[2];
+  cudaLaunchConfig_t cfg = launch_config_quad<EPI>(s, grid, at);
+  cudaError_t e = cudaLaunchKernelEx(&cfg, gemm_quad_kernel<EPI>, ta, tb, p);
+  lc::record_launch(ctx, "gemm_bf16_quad_n256");
+  if (e != cudaSuccess) return lc::cuda_fail(e, "gemm quad launch");
+  e = cudaGetLastError();
+  if (e != cudaSuccess) return lc::cuda_fail(e, "gemm quad launch");
+  return LC_OK;
+}
+
 int64_t ceil_div(int64_t a, int64_t b) { return (a + b - 1) / b; }
 
 }  // namespace
@@ -1763,8 +1843,8 @@ struct Planned {
   KParams p{};
   CUtensorMap ta, tb;
   int bn = 64;
-  bool tf32x3 = false, pair = false, two_sm = false;
-  int64_t pair_clusters = 0, two_sm_clusters = 0, tiles = 0, units = 0, splits = 1, M = 0, N = 0;
+  bool tf32x3 = false, pair = false, two_sm = false, quad = false;
+  int64_t pair_clusters = 0, two_sm_clusters = 0, quad_clusters = 0, tiles = 0, units = 0, splits = 1, M = 0, N = 0;
   bool swap = false;
 };
 
@@ -1857,6 +1937,21 @@ lc_status plan_gemm(lc_context* ctx, const lc::GemmProblem& pr, lc_contract_plan
     pair_clusters = std::min<int64_t>({tiles, (int64_t)cap, (ctx->sm_count - pr.reserve_sms) / 2});
   }
   const bool pair = pair_clusters > 0;
+  // A 2-way split of a 256-wide tile with at least 256 rows runs on clusters of 4: two CTA pairs
+  // with cta_group::2 MMAs over 256 x 256 tiles, one pair per K half, exchanging partials like a
+  // CTA pair.  Each CTA loads 128 rows of A and half of B^T per stage, a third less than a
+  // 128 x 256 tile on one SM, which is what bounds the grouped skinny products.
+  static const bool env_no_quad = [] {
+    const char* e = getenv("LC_GEMM_QUAD");  // tuning override: "0" keeps such products on CTA pairs
+    return e != nullptr && e[0] == '0';
+  }();
+  int64_t quad_clusters = 0;
+  if (pair && bn == 256 && M >= 256 && !env_no_quad) {
+    const int cap = pr.epi == 0 ? capacity_quad<0>(ctx) : capacity_quad<1>(ctx);
+    quad_clusters = std::min<int64_t>({ceil_div(M, 256) * ceil_div(N, bn) * (int64_t)pr.batch, (int64_t)cap,
+                                       (ctx->sm_count - pr.reserve_sms) / 4});
+  }
+  const bool quad = quad_clusters > 0;
   // 256-row tiles over CTA pairs (cta_group::2 MMAs): each CTA reads 128 rows of A and half of
   // the tile's B^T, a third less operand traffic per output than a 128 x 256 tile on one SM.
   // Taken for unsplit BN = 256 products with enough tiles to give every pair of SMs work.
@@ -1873,8 +1968,8 @@ lc_status plan_gemm(lc_context* ctx, const lc::GemmProblem& pr, lc_contract_plan
     two_sm_clusters = std::min<int64_t>({tiles2, (int64_t)cap, sm_pairs});
   }
   const bool two_sm = two_sm_clusters > 0;
-  const int64_t tiles_m_eff = two_sm ? tiles_m2 : tiles_m;
-  const int64_t units_eff = two_sm ? tiles2 : units;
+  const int64_t tiles_m_eff = (two_sm || quad) ? tiles_m2 : tiles_m;
+  const int64_t units_eff = two_sm ? tiles2 : quad ? tiles2 * splits : units;
   if (units >= (1ll << 31) || k_tiles >= (1ll << 31)) return fail(LC_ERR_INVALID_ARGUMENT, "problem too large");
 
   if (operand_major(A) < 0 || operand_major(B) < 0) return fail(LC_ERR_INVALID_ARGUMENT, "operand has no unit stride");
@@ -1911,7 +2006,8 @@ lc_status plan_gemm(lc_context* ctx, const lc::GemmProblem& pr, lc_contract_plan
   if (st) return st;
   if (!b_mn) {
     uint64_t rs = B.mn > 1 ? B.mn_stride * es : ((B.k * es + 15) / 16) * 16;
-    st = make_map(&tb, bbase, pr.in_dtype, B.k, B.mn, pr.batch, rs, bstride(B, rs * B.mn), epr, two_sm ? bn / 2 : bn);
+    st = make_map(&tb, bbase, pr.in_dtype, B.k, B.mn, pr.batch, rs, bstride(B, rs * B.mn), epr,
+                  (two_sm || quad) ? bn / 2 : bn);
   } else {
     uint64_t rs = B.k > 1 ? B.k_stride * es : ((B.mn * es + 15) / 16) * 16;
     st = make_map(&tb, bbase, pr.in_dtype, B.mn, B.k, pr.batch, rs, bstride(B, rs * B.k), epr, epr, tf32x3);
@@ -1946,7 +2042,7 @@ lc_status plan_gemm(lc_context* ctx, const lc::GemmProblem& pr, lc_contract_plan
   p.a_mn = a_mn;
   p.b_mn = b_mn;
   const uint32_t fmt = tf32x3 ? 2u : (pr.in_dtype == LC_BF16 ? 1u : 0u);
-  p.idesc = lcd::make_idesc(fmt, two_sm ? 256 : 128, bn, a_mn, b_mn);
+  p.idesc = lcd::make_idesc(fmt, (two_sm || quad) ? 256 : 128, bn, a_mn, b_mn);
   p.c_dtype = pr.c_dtype;
   p.relu = pr.relu;
   p.c = pr.c;
@@ -1995,7 +2091,9 @@ lc_status plan_gemm(lc_context* ctx, const lc::GemmProblem& pr, lc_contract_plan
   out->pair_clusters = pair_clusters;
   out->two_sm = two_sm;
   out->two_sm_clusters = two_sm_clusters;
-  out->tiles = two_sm ? tiles2 : tiles;
+  out->quad = quad;
+  out->quad_clusters = quad_clusters;
+  out->tiles = (two_sm || quad) ? tiles2 : tiles;
   out->units = units_eff;
   out->splits = splits;
   out->M = (int64_t)M;
@@ -2082,10 +2180,13 @@ lc_status gemm_run(lc_context* ctx, cudaStream_t s, const GemmProblem& pr, lc_co
       }
     }
   }
-  const int grid = pair ? (int)(2 * pair_clusters)
+  const int grid = pl.quad ? (int)(4 * pl.quad_clusters)
+                   : pair ? (int)(2 * pair_clusters)
                    : pl.two_sm ? (int)(2 * pl.two_sm_clusters)
                                : (int)std::max<int64_t>(1, std::min<int64_t>(units, ctx->sm_count - pr.reserve_sms));
-  if (pl.two_sm) {
+  if (pl.quad) {
+    st = pr.epi == 0 ? launch_quad<0>(ctx, s, ta, tb, p, grid) : launch_quad<1>(ctx, s, ta, tb, p, grid);
+  } else if (pl.two_sm) {
     st = pr.epi == 0   ? launch_2sm<0>(ctx, s, ta, tb, p, grid)
          : pr.epi == 1 ? launch_2sm<1>(ctx, s, ta, tb, p, grid)
                        : launch_2sm<2>(ctx, s, ta, tb, p, grid);

@@ -279,6 +279,14 @@ __device__ __forceinline__ uint32_t leader_addr(uint32_t smem_addr) {
   return r;
 }
 
+// The same location in the cluster CTA of rank `leader` (the pair's even CTA when a cluster
+// holds several pairs).
+__device__ __forceinline__ uint32_t rank_addr(uint32_t smem_addr, uint32_t leader) {
+  uint32_t r;
+  asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(r) : "r"(smem_addr), "r"(leader));
+  return r;
+}
+
 __device__ __forceinline__ void tmem_alloc_2sm(uint32_t* dst_smem, uint32_t ncols) {
   asm volatile("tcgen05.alloc.cta_group::2.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(dst_smem)),
                "r"(ncols)
@@ -313,6 +321,16 @@ __device__ __forceinline__ void umma_commit_2sm_both(uint64_t* bar) {
       "mov.b16 m, 3;\n\t"
       "tcgen05.commit.cta_group::2.mbarrier::arrive::one.shared::cluster.multicast::cluster.b64 [%0], m;\n\t}" ::"r"(
           smem_u32(bar))
+      : "memory");
+}
+
+// Same for the pair of cluster ranks `leader` and `leader + 1` (leader even).
+__device__ __forceinline__ void umma_commit_2sm_pair(uint64_t* bar, uint32_t leader) {
+  const uint16_t mask = (uint16_t)(3u << leader);
+  asm volatile(
+      "tcgen05.commit.cta_group::2.mbarrier::arrive::one.shared::cluster.multicast::cluster.b64 [%0], %1;" ::"r"(
+          smem_u32(bar)),
+      "h"(mask)
       : "memory");
 }
 

@@ -132,7 +132,8 @@ def test_grouped_product_as_the_one_stage_step_plans_it(ctx, weights, which):
     """A stage holding every layer runs four microbatches as one [256, 8192] x [8192, 8192]
     product, pinned to the one-microbatch product's split (2) and orientation (C^T = W^T H^T) on a
     256-wide tile, so each weight tile is read once for the whole group.  It must equal the four
-    one-microbatch products bit for bit and the oracle within tolerance."""
+    one-microbatch products bit for bit (and the same product on 128 x 256 CTA-pair tiles,
+    LC_GEMM_QUAD=0, which the pipeline grouping test compares) and the oracle within tolerance."""
     w, wbits = weights
     fwd = which == "forward"
     rows = 256
@@ -144,7 +145,8 @@ def test_grouped_product_as_the_one_stage_step_plans_it(ctx, weights, which):
     lb.encode_gemm_fused(ctx, None, 1.0, a, b, 0.0, grouped, epi, aux=None if fwd else h, tile_n=256, splits=2,
                          swap=1)
     ctx.sync()
-    assert launched(ctx, "gemm_bf16_pair_n256", 1), ctx.debug_launches()[-4:]
+    # 256 x 256 tiles on clusters of 4 (two CTA pairs with cta_group::2 MMAs, one per K half)
+    assert launched(ctx, "gemm_bf16_quad_n256", 1), ctx.debug_launches()[-4:]
     single = torch.empty_like(grouped)
     for j in range(4):
         sl = slice(64 * j, 64 * j + 64)

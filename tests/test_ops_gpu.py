@@ -471,9 +471,21 @@ def test_contract_bf16(ctx, m, n, k):
                                              (2560, 2304, 320, False, torch.float16)])
 def test_contract_two_sm_tiles(ctx, m, n, k, bt, dtype):
     """Products with a 256 x 256 tile for every pair of SMs run on CTA pairs with cta_group::2
-    MMAs (each CTA holds 128 rows of A and half of B^T): both B layouts, an M tail, f16."""
-    rel, *_ = run_gemm_case(ctx, m, n, k, dtype=dtype, bt=bt, seed=m + k)
-    assert rel <= BF16_TOL, rel
+    MMAs (each CTA holds 128 rows of A and half of B^T): both B layouts, an M tail, f16.  f16
+    products reach the tensor cores through the Backend slot's gemm (the op API rounds f16 once
+    from a double-float dot instead)."""
+    if dtype == torch.bfloat16:
+        rel, *_ = run_gemm_case(ctx, m, n, k, dtype=dtype, bt=bt, seed=m + k)
+        assert rel <= BF16_TOL, rel
+    else:
+        a = dev(data.uniform(m + k, (m, k))).half()
+        b = dev(data.uniform(m + k + 1, (k, n))).half()
+        c = torch.zeros(m, n, device="cuda", dtype=torch.float16)
+        lb.backend_gemm(ctx, a, b, c, 1.0, 0.0)
+        ctx.sync()
+        exact = (a.double() @ b.double()).cpu().numpy()
+        rel = np.abs(c.double().cpu().numpy() - exact).max() / np.abs(exact).max()
+        assert rel <= BF16_TOL, rel
     assert "gemm_bf16_2sm_n256" in ctx.debug_launches()[-4:]
 
 
@@ -675,3 +687,72 @@ def test_backend_gemm_contract_rules(ctx):
         lb.backend_gemm(ctx, a, b, lb.View.raw(a, 0, [5, 3], [3, 1]), 1.0, 0.0)
     with pytest.raises(lb.UnsupportedLayout):
         lb.backend_gemm(ctx, a, b, lb.View.raw(c, 1, [5, 3], [3, 1]), 1.0, 0.0)
+
+
+# ------------------------------------------------------------------------------------------------
+# f16: one rounding of a double-float dot (shaders/contraction.metal:445-755), bit-exact against
+# the oracle's restatement
+# ------------------------------------------------------------------------------------------------
+
+def f16_bits(t) -> np.ndarray:
+    return t.detach().contiguous().view(torch.int16).cpu().numpy().view(np.uint16)
+
+
+@pytest.mark.parametrize("m,n,k,alpha,beta,at,bt", [(1, 1, 1, 1.0, 0.0, False, False), (37, 53, 300, 1.0, 0.0, False, False),
+                                                    (64, 40, 1000, -0.75, 0.5, True, False),
+                                                    (33, 17, 4097, 2.0, -1.0, False, True),
+                                                    (300, 200, 64, 1.0, 1.0, True, True)])
+def test_contract_f16_rounds_once_bit_exact(ctx, m, n, k, alpha, beta, at, bt):
+    rng = np.random.default_rng(m * 7 + k)
+    a = rng.standard_normal((k, m) if at else (m, k)).astype(np.float16)
+    b = rng.standard_normal((n, k) if bt else (k, n)).astype(np.float16)
+    c0 = rng.standard_normal((m, n)).astype(np.float16)
+    ta = dev(a).t() if at else dev(a)
+    tb = dev(b).t() if bt else dev(b)
+    tc = dev(c0)
+    assert lb.plan_contract(ctx, alpha, (ta, "ik"), (tb, "kj"), beta, (tc, "ij"))["kind"] == "General"
+    lb.contract(ctx, alpha, (ta, "ik"), (tb, "kj"), beta, (tc, "ij"))
+    want = c0.view(np.uint16).copy()
+    O.contract_f16(a.view(np.uint16), b.view(np.uint16), want, alpha, beta,
+                   a_strides=(1, m) if at else None, b_strides=(1, k) if bt else None, k=k)
+    assert np.array_equal(f16_bits(tc), want)
+    assert "contract_general_f16" in ctx.debug_launches()[-2:]
+
+
+def test_contract_f16_multi_stride_in_place(ctx):
+    """A permuted, batched f16 contraction (two strides per group) runs without staging copies
+    and equals the oracle's per-batch products bit for bit."""
+    rng = np.random.default_rng(9)
+    a = rng.standard_normal((6, 8, 10, 12)).astype(np.float16)   # labels b m k1 k2 -> "bmcd"
+    bm = rng.standard_normal((12, 6, 10, 7)).astype(np.float16)  # labels k2 b k1 n -> "dbce"
+    ta, tb = dev(a), dev(bm)
+    tc = torch.zeros((7, 6, 8), dtype=torch.float16, device="cuda")  # "ebm"
+    plan = lb.plan_contract(ctx, 1.0, (ta, "bmcd"), (tb, "dbce"), 0.0, (tc, "ebm"))
+    assert plan["kind"] == "General"
+    lb.contract(ctx, 1.0, (ta, "bmcd"), (tb, "dbce"), 0.0, (tc, "ebm"))
+    assert not any(n.startswith("strided_copy") or n.startswith("copy") for n in ctx.debug_launches()[-3:])
+    got = f16_bits(tc)
+    for bb in range(6):
+        A = np.ascontiguousarray(a[bb].reshape(8, 120))                        # k = (c, d)
+        B = np.ascontiguousarray(bm[:, bb].transpose(1, 0, 2).reshape(120, 7))  # k = (c, d)
+        want = np.zeros((8, 7), np.uint16)
+        O.contract_f16(A.view(np.uint16), B.view(np.uint16), want, 1.0, 0.0)
+        assert np.array_equal(got[:, bb, :].T, want), bb
+
+
+def test_contract_f16_scale_rounds_once(ctx):
+    """tests/contraction_test.rs:445-470: K = 0 and beta = -0.999 take f16 0x0DDC to 0x8DDB."""
+    a = torch.zeros((4, 0), dtype=torch.float16, device="cuda")
+    b = torch.zeros((0, 3), dtype=torch.float16, device="cuda")
+    c0 = np.random.default_rng(3).standard_normal((4, 3)).astype(np.float16)
+    c0.view(np.uint16)[0, 0] = 0x0DDC
+    c0[0, 1] = np.inf
+    c0[0, 2] = np.nan
+    tc = dev(c0)
+    lb.contract(ctx, 1.0, (a, "ik"), (b, "kj"), -0.999, (tc, "ij"))
+    got = f16_bits(tc)
+    assert got[0, 0] == 0x8DDB and got[0, 1] == 0xFC00 and np.isnan(tc[0, 2].item())
+    want = c0.view(np.uint16).copy()
+    O.contract_f16(np.zeros((4, 0), np.uint16), np.zeros((0, 3), np.uint16), want, 1.0, -0.999, k=0)
+    ok = (got == want) | (np.isnan(got.view(np.float16)) & np.isnan(want.view(np.float16)))
+    assert ok.all()
