@@ -465,9 +465,10 @@ def main():
         extras = op_figures(hbm_peak, tc_peak)
     roof_one = None
     if rank == 0:
-        # the dominant kernel: the grouped product on one stage, the one-microbatch product on several
+        # the dominant kernel: every stage runs its microbatches in groups of four, one product per
+        # layer over 256 rows; the one-microbatch product is reported beside it
         roof_one = product_roofline(hbm_peak, tc_peak, MB, grouped=False)
-        roof = product_roofline(hbm_peak, tc_peak, 4 * MB, grouped=True) if world == 1 else roof_one
+        roof = product_roofline(hbm_peak, tc_peak, 4 * MB, grouped=True)
 
     uid = None
     if world > 1:
@@ -565,8 +566,7 @@ def main():
             "step_tflops": STEP_FLOP / (ms / args.steps * 1e-3) / 1e12,
             "step_frac_of_sustained_bf16": STEP_FLOP / (ms / args.steps * 1e-3) / 1e12 / tc_sustained,
         }
-        if world == 1:
-            line["roofline_one_microbatch"] = roof_one
+        line["roofline_one_microbatch"] = roof_one
         line["stage_trace"] = gathered
         if cpu_v is not None:
             line["cpu_baseline"] = {"value": cpu_v, "unit": "samples/s", "cores": 1, "kind": "port",
